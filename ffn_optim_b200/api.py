@@ -1,0 +1,175 @@
+"""Public API: ``ffn``, ``prepare_ffn`` and ``PreparedFFN`` (mirrors ops/api.py of the reference).
+
+Same call signatures, argument meaning, return value (a view of a reused output buffer
+that the next run overwrites) and error types.  Execution goes through the C ABI of the
+sm_100a library; there is no CPU or torch fallback -- CPU tensors are rejected and a
+missing library raises :class:`KernelCompilationError`.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from time import perf_counter
+
+from . import _lib
+from .host.dispatch import Selection, kernel_provenance
+from .host.inputs import prepare_storage, validate_tensors
+from .host.tiling import make_plan
+
+
+class KernelCompilationError(RuntimeError):
+    """The CUDA library could not be loaded or the kernel could not be set up
+    (reference ops/api.py:9-14 wraps DSL compile failures the same way)."""
+
+
+@dataclass
+class PreparedFFN:
+    """A prepared fused FFN that can be launched repeatedly (reference ops/api.py:17-45).
+
+    ``storage`` is ``(x2d, w1, w2, hidden, out, workspace, counters, flags, status)`` on
+    one CUDA device.  :meth:`run` launches one kernel on the preparation stream and returns
+    ``out[:M, :N]`` viewed as ``(*x.shape[:-1], N)``; the view shares storage with the
+    prepared buffer and the next run overwrites it.  Runs are asynchronous; :meth:`check`
+    synchronises and raises if the kernel reported an error.
+    """
+
+    plan: object
+    storage: tuple
+    handle: object
+    provenance: dict
+    preparation: dict
+    stream: object
+
+    def _output_view(self):
+        p = self.plan.problem
+        return self.storage[4][:, :p.n].view(p.output_shape)
+
+    def load_input(self, x):
+        """Copies a new X (same shape/dtype; device tensor or pinned host tensor) into storage."""
+        p = self.plan.problem
+        if tuple(x.shape) != tuple(p.input_shape) or x.dtype != self.storage[0].dtype:
+            raise ValueError("load_input: x must have the prepared shape and dtype")
+        self.storage[0][:, :p.k].copy_(x.reshape(p.m, p.k), non_blocking=True)
+
+    def run(self, x=None):
+        """One FFN launch.  The returned view is overwritten by the next run."""
+        import torch
+
+        if self.handle is None:
+            raise RuntimeError("PreparedFFN has been closed")
+        with torch.cuda.device(self.storage[0].device):
+            if torch.cuda.current_stream() != self.stream:
+                raise RuntimeError("PreparedFFN must run on its preparation stream; concurrent reuse is unsupported")
+            if x is not None:
+                self.load_input(x)
+            rc = _lib.load().ffn_b200_run(self.handle, ctypes.c_void_p(self.stream.cuda_stream))
+            if rc != _lib.OK:
+                raise RuntimeError(f"ffn_b200_run: {_lib.strerror(rc)}")
+        return self._output_view()
+
+    def status(self):
+        """Synchronises the stream and returns the kernel's status words [code, cta, aux, 0]."""
+        self.stream.synchronize()
+        return [int(v) for v in self.storage[8].tolist()]
+
+    def check(self):
+        """Raises RuntimeError if any launch since the last reset reported a device error."""
+        st = self.status()
+        if st[0] != 0:
+            self.reset()
+            msg = _lib.KERNEL_ERRORS.get(st[0], f"error {st[0]}")
+            raise RuntimeError(f"fused FFN kernel failed: {msg} (cta {st[1]}, aux {st[2]})")
+        return True
+
+    def reset(self):
+        """Clears counters, flags and status and restarts the launch epoch."""
+        rc = _lib.load().ffn_b200_reset(self.handle, ctypes.c_void_p(self.stream.cuda_stream))
+        if rc != _lib.OK:
+            raise RuntimeError(f"ffn_b200_reset: {_lib.strerror(rc)}")
+
+    def set_wait_limit(self, seconds: float):
+        """Upper bound of every in-kernel wait; on expiry the kernel reports an error."""
+        rc = _lib.load().ffn_b200_set_wait_limit(self.handle, int(seconds * 1e9))
+        if rc != _lib.OK:
+            raise ValueError(f"set_wait_limit: {_lib.strerror(rc)}")
+
+    def set_fault_injection(self, mode: int):
+        """Test hook (1 = readiness waits can never be satisfied); see ffn_b200_set_fault_injection."""
+        rc = _lib.load().ffn_b200_set_fault_injection(self.handle, int(mode))
+        if rc != _lib.OK:
+            raise ValueError(f"set_fault_injection: {_lib.strerror(rc)}")
+
+    def close(self):
+        if self.handle is not None:
+            _lib.load().ffn_b200_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+def _map_prepare_error(rc):
+    msg = _lib.strerror(rc)
+    if rc in (_lib.ERR_INVALID, _lib.ERR_ALIGNMENT, _lib.ERR_TOO_LARGE):
+        return ValueError(f"prepare_ffn: {msg}")
+    if rc == _lib.ERR_DEVICE:
+        return RuntimeError(f"prepare_ffn: {msg}")
+    return KernelCompilationError(f"prepare_ffn: {msg}")
+
+
+def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", block_num=None,
+                layout="linear", gelu="rational"):
+    """Validates, plans and prepares storage and the launch handle without launching the FFN
+    (reference ops/api.py:48-89).
+
+    ``block_num`` is the persistent CTA count, at most the device's SM count (default: all
+    SMs).  ``gelu`` selects the epilogue GELU: 'rational' (the reference kernel's clipped
+    rational erf) or 'erf' (CUDA ``erff``).  Storage copies are device work timed
+    separately as ``preparation['auxiliary_device_interval_ms']``.
+    """
+    import torch
+
+    p = validate_tensors(x, weight1, weight2, layout=layout, require_cuda=True)
+    selection = Selection(up_impl, down_impl)
+    try:
+        lib = _lib.load()
+    except (OSError, RuntimeError) as exc:
+        raise KernelCompilationError(f"{type(exc).__name__}: {exc}") from exc
+    props = torch.cuda.get_device_properties(x.device)
+    plan = make_plan(p, selection, block_num, gelu=gelu, sm_count=props.multi_processor_count)
+    if (props.major, props.minor) != (10, 0):
+        raise RuntimeError("This implementation targets B200 (sm_100) only")
+    if plan.block_num > props.multi_processor_count:
+        raise ValueError("Persistent grid requires block_num <= SM count")
+    with torch.cuda.device(x.device):
+        stream = torch.cuda.current_stream()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        storage = prepare_storage(x, weight1, weight2, plan)
+        end.record()
+        end.synchronize()
+        auxiliary_ms = start.elapsed_time(end)
+        x2d, w1, w2, hidden, out, ws, counters, flags, status = storage
+        bufs = _lib.Buffers(x2d.data_ptr(), x2d.stride(0), w1.data_ptr(), w1.stride(0), w2.data_ptr(), w2.stride(0),
+                            hidden.data_ptr(), hidden.stride(0), out.data_ptr(), out.stride(0), ws.data_ptr(),
+                            counters.data_ptr(), flags.data_ptr(), status.data_ptr())
+        prob = _lib.Problem(p.m, p.k, p.h, p.n, _lib.DTYPES[p.dtype], _lib.DOWN_IMPL_CODES[down_impl],
+                            _lib.GELU_CODES[gelu], plan.block_num, props.multi_processor_count)
+        handle = ctypes.c_void_p()
+        before = perf_counter()
+        rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), x.device.index or 0, ctypes.byref(handle))
+        if rc != _lib.OK:
+            raise _map_prepare_error(rc)
+        preparation = {"auxiliary_device_interval_ms": auxiliary_ms,
+                       "compile_wall_ms": (perf_counter() - before) * 1000}
+    provenance = kernel_provenance(down_impl)
+    provenance["plan"] = plan.kernel
+    return PreparedFFN(plan, storage, handle, provenance, preparation, stream)
+
+
+def ffn(x, weight1, weight2, **configuration):
+    """Y = GELU(X @ weight1.T) @ weight2.T; no bias, no autograd (reference ops/api.py:92-94)."""
+    return prepare_ffn(x, weight1, weight2, **configuration).run()

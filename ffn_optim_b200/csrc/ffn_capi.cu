@@ -1,0 +1,455 @@
+// C ABI of the B200 fused FFN (declarations and reference citations in include/ffn_b200.h).
+//
+// Host responsibilities, all without device allocation:
+//   * planning   -- tile shape, swap-AB choice, Stream-K split, scratch sizes
+//                   (reference: ops/host/tiling.py:58-74, ops/host/dispatch.py:42-66);
+//   * preparing  -- device / block_num checks and TMA tensor-map encoding
+//                   (reference: ops/api.py:48-89, ops/host/dispatch.py:97-116);
+//   * running    -- one cooperative launch of the persistent fused kernel per call
+//                   (reference: ops/api.py:37-45).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <new>
+
+#include "../../include/ffn_b200.h"
+#include "ffn_kernel.cuh"
+
+namespace {
+
+using ffnb200::Params;
+using ffnb200::PhaseSched;
+using KernelFn = void (*)(const Params);
+
+struct Variant {
+  int bn, stages;
+  bool swap;
+};
+// 0: prefill tiles 128x256, 1: 128x128 for small grids, 2/3: swap-AB decode tiles.
+constexpr Variant kVariants[] = {{256, 4, false}, {128, 6, false}, {16, 8, true}, {64, 8, true}};
+constexpr int kNumVariants = 4;
+
+template <int BN, int ST, bool SW>
+KernelFn pick_kernel(int bf16, int gelu) {
+  using namespace ffnb200;
+  if (bf16) return gelu ? ffn_fused_kernel<BN, ST, SW, true, 1> : ffn_fused_kernel<BN, ST, SW, true, 0>;
+  return gelu ? ffn_fused_kernel<BN, ST, SW, false, 1> : ffn_fused_kernel<BN, ST, SW, false, 0>;
+}
+KernelFn kernel_for(int variant, int bf16, int gelu) {
+  switch (variant) {
+    case 0: return pick_kernel<256, 4, false>(bf16, gelu);
+    case 1: return pick_kernel<128, 6, false>(bf16, gelu);
+    case 2: return pick_kernel<16, 8, true>(bf16, gelu);
+    case 3: return pick_kernel<64, 8, true>(bf16, gelu);
+  }
+  return nullptr;
+}
+int smem_for(int variant) {
+  switch (variant) {
+    case 0: return ffnb200::Layout<256, 4, false>::kSmem;
+    case 1: return ffnb200::Layout<128, 6, false>::kSmem;
+    case 2: return ffnb200::Layout<16, 8, true>::kSmem;
+    case 3: return ffnb200::Layout<64, 8, true>::kSmem;
+  }
+  return 0;
+}
+int tmem_cols_for(int variant) {
+  const int c = 2 * kVariants[variant].bn;
+  return c < 32 ? 32 : c;
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+struct PhaseInput {
+  int64_t rows, cols, depth;
+};
+
+// Fills one phase's schedule.  split=true applies the Stream-K tail split of the reference
+// (ops/kernel/ffn.py:642-665): sk = T mod C tail tiles, their sk*L k-blocks spread as
+// q = floor(sk*L / C) per CTA with the first (sk*L mod C) CTAs taking one more.
+int phase_plan(const PhaseInput& in, int bn, int C, bool split, ffn_b200_phase_plan* out) {
+  const int64_t tr = cdiv(in.rows, ffnb200::kBM);
+  const int64_t tq = cdiv(in.cols, bn);
+  const int64_t T = tr * tq;
+  const int64_t L = cdiv(in.depth, ffnb200::kBK);
+  if (T >= (int64_t(1) << 31) || tr >= (int64_t(1) << 31)) return FFN_B200_ERR_TOO_LARGE;
+  out->tiles_r = static_cast<int32_t>(tr);
+  out->tiles_q = static_cast<int32_t>(tq);
+  out->tiles = static_cast<int32_t>(T);
+  out->k_blocks = static_cast<int32_t>(L);
+  out->group = static_cast<int32_t>(tr < 16 ? tr : 16);
+  if (split) {
+    const int64_t sk = T % C;
+    const int64_t iters = sk * L;
+    out->sk_tiles = static_cast<int32_t>(sk);
+    out->dp_tiles = static_cast<int32_t>(T - sk);
+    out->sk_iters = static_cast<int32_t>(iters / C);
+    out->sk_rem = static_cast<int32_t>(iters % C);
+  } else {
+    out->sk_tiles = 0;
+    out->dp_tiles = static_cast<int32_t>(T);
+    out->sk_iters = 0;
+    out->sk_rem = 0;
+  }
+  return FFN_B200_OK;
+}
+
+int query_sm_count(int* sm) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FFN_B200_ERR_CUDA;
+  if (cudaDeviceGetAttribute(sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return FFN_B200_ERR_CUDA;
+  return FFN_B200_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode ? FFN_B200_OK : FFN_B200_ERR_CUDA;
+}
+
+// 2-D row-major tensor [outer, inner] with `pitch` elements per row; 128B-swizzled boxes.
+int encode_2d(CUtensorMap* tm, const void* base, int dtype, int64_t inner, int64_t outer, int64_t pitch,
+              uint32_t box_inner, uint32_t box_outer) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch) * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == FFN_B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = g_encode(tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FFN_B200_OK : FFN_B200_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+struct ffn_b200_handle {
+  ffn_b200_problem prob;
+  ffn_b200_plan plan;
+  ffn_b200_buffers buf;
+  int device;
+  KernelFn kernel;
+  Params params;
+  unsigned epoch;
+  unsigned epoch_limit;
+};
+
+extern "C" {
+
+int ffn_b200_abi_version(void) { return FFN_B200_ABI_VERSION; }
+
+const char* ffn_b200_strerror(int code) {
+  switch (code) {
+    case FFN_B200_OK: return "ok";
+    case FFN_B200_ERR_INVALID: return "invalid argument";
+    case FFN_B200_ERR_NOT_APPLICABLE: return "Stream-K candidate has no remainder tiles or fewer than two K tiles";
+    case FFN_B200_ERR_UNAVAILABLE: return "implementation not available (full_load_a / full_load_b)";
+    case FFN_B200_ERR_DEVICE: return "device is not sm_100 or block_num exceeds the SM count";
+    case FFN_B200_ERR_CUDA: return "CUDA call failed";
+    case FFN_B200_ERR_ALIGNMENT: return "buffer base not 16-byte aligned or pitch not a multiple of 8 elements";
+    case FFN_B200_ERR_TOO_LARGE: return "problem does not fit one launch";
+  }
+  return "unknown error";
+}
+
+int ffn_b200_device_info(int device, int* sm_count, int* cc_major, int* cc_minor) {
+  if (!sm_count || !cc_major || !cc_minor) return FFN_B200_ERR_INVALID;
+  if (cudaDeviceGetAttribute(sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(cc_major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(cc_minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) {
+    cudaGetLastError();
+    return FFN_B200_ERR_CUDA;
+  }
+  return FFN_B200_OK;
+}
+
+int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
+  if (!pr || !out) return FFN_B200_ERR_INVALID;
+  // Shape contract of ops/host/inputs.py:38-53.
+  if (pr->m <= 0 || pr->k <= 0 || pr->h <= 0 || pr->n <= 0) return FFN_B200_ERR_INVALID;
+  if (pr->k > 65535 || pr->h > 65535 || pr->n > 65535 || pr->m > (int64_t(1) << 31) - 16)
+    return FFN_B200_ERR_INVALID;
+  if (pr->dtype != FFN_B200_F16 && pr->dtype != FFN_B200_BF16) return FFN_B200_ERR_INVALID;
+  if (pr->gelu != FFN_B200_GELU_RATIONAL && pr->gelu != FFN_B200_GELU_ERF) return FFN_B200_ERR_INVALID;
+  if (pr->down_impl < 0 || pr->down_impl > 3) return FFN_B200_ERR_INVALID;
+  if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_A || pr->down_impl == FFN_B200_DOWN_FULL_LOAD_B)
+    return FFN_B200_ERR_UNAVAILABLE;
+  int sm = pr->sm_count;
+  if (sm <= 0) {
+    const int rc = query_sm_count(&sm);
+    if (rc) return rc;
+  }
+  const int C = pr->block_num > 0 ? pr->block_num : sm;
+  if (C < 1 || C > 65535 || pr->block_num < 0) return FFN_B200_ERR_INVALID;
+
+  std::memset(out, 0, sizeof(*out));
+  int variant;
+  if (pr->m <= 16) {
+    variant = 2;
+  } else if (pr->m <= 64) {
+    variant = 3;
+  } else {
+    const int64_t t256 = cdiv(pr->m, 128) * cdiv(pr->h, 256);
+    variant = t256 >= 2 * static_cast<int64_t>(C) ? 0 : 1;
+  }
+  const Variant& v = kVariants[variant];
+  const PhaseInput up = v.swap ? PhaseInput{pr->h, pr->m, pr->k} : PhaseInput{pr->m, pr->h, pr->k};
+  const PhaseInput dn = v.swap ? PhaseInput{pr->n, pr->m, pr->h} : PhaseInput{pr->m, pr->n, pr->h};
+
+  // Up phase: data-parallel, with the tail wave split along K when whole tiles would leave
+  // more than a tenth of the CTAs idle in the last wave (a schedule choice only).
+  ffn_b200_phase_plan probe;
+  int rc = phase_plan(up, v.bn, C, false, &probe);
+  if (rc) return rc;
+  const int64_t waves = cdiv(probe.tiles, C);
+  const bool up_split = (probe.tiles % C) != 0 && probe.k_blocks >= 2 &&
+                        static_cast<double>(probe.tiles) < 0.9 * static_cast<double>(waves * C);
+  rc = phase_plan(up, v.bn, C, up_split, &out->up);
+  if (rc) return rc;
+
+  const bool streamk = pr->down_impl == FFN_B200_DOWN_STREAMK;
+  rc = phase_plan(dn, v.bn, C, streamk, &out->down);
+  if (rc) return rc;
+  if (streamk && (out->down.tiles % C == 0 || out->down.k_blocks < 2)) return FFN_B200_ERR_NOT_APPLICABLE;
+  if (static_cast<int64_t>(out->up.sk_tiles) * out->up.k_blocks >= (int64_t(1) << 31) ||
+      static_cast<int64_t>(out->down.sk_tiles) * out->down.k_blocks >= (int64_t(1) << 31))
+    return FFN_B200_ERR_TOO_LARGE;
+
+  out->variant = variant;
+  out->swap_ab = v.swap ? 1 : 0;
+  out->tile_m = ffnb200::kBM;
+  out->tile_n = v.bn;
+  out->tile_k = ffnb200::kBK;
+  out->stages = v.stages;
+  out->block_num = C;
+  out->tmem_cols = tmem_cols_for(variant);
+  out->smem_bytes = smem_for(variant);
+  out->workspace_floats = 2ll * C * ffnb200::kBM * v.bn;
+  out->counter_words = v.swap ? out->up.tiles_q : out->up.tiles_r;
+  out->flag_words = 2ll * C;
+  out->status_words = 4;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int device, ffn_b200_handle** out) {
+  if (!pr || !b || !out) return FFN_B200_ERR_INVALID;
+  *out = nullptr;
+  int sm = 0, ccmaj = 0, ccmin = 0;
+  int rc = ffn_b200_device_info(device, &sm, &ccmaj, &ccmin);
+  if (rc) return rc;
+  if (ccmaj != 10 || ccmin != 0) return FFN_B200_ERR_DEVICE;
+  ffn_b200_problem prob = *pr;
+  if (prob.sm_count <= 0) prob.sm_count = sm;
+  if (prob.block_num > sm) return FFN_B200_ERR_DEVICE;  // co-residency (ops/api.py:63-64)
+  ffn_b200_plan plan;
+  rc = ffn_b200_make_plan(&prob, &plan);
+  if (rc) return rc;
+  if (plan.block_num > sm) return FFN_B200_ERR_DEVICE;
+
+  // Buffers: TMA needs 16-byte aligned bases and pitches.
+  const void* bases[] = {b->x, b->w1, b->w2, b->hidden, b->y, b->workspace};
+  for (const void* p : bases)
+    if (!p) return FFN_B200_ERR_INVALID;
+  for (const void* p : bases)
+    if (!aligned16(p)) return FFN_B200_ERR_ALIGNMENT;
+  if (!b->counters || !b->flags || !b->status) return FFN_B200_ERR_INVALID;
+  const int64_t pitches[] = {b->ldx, b->ldw1, b->ldw2, b->ldh, b->ldy};
+  for (int64_t p : pitches)
+    if (p <= 0 || (p % 8) != 0) return FFN_B200_ERR_ALIGNMENT;
+  if (b->ldx < prob.k || b->ldw1 < prob.k || b->ldw2 < prob.h || b->ldh < prob.h || b->ldy < prob.n)
+    return FFN_B200_ERR_INVALID;
+
+  rc = get_encode();
+  if (rc) return rc;
+
+  auto* h = new (std::nothrow) ffn_b200_handle();
+  if (!h) return FFN_B200_ERR_INVALID;
+  h->prob = prob;
+  h->plan = plan;
+  h->buf = *b;
+  h->device = device;
+  h->kernel = kernel_for(plan.variant, prob.dtype == FFN_B200_BF16, prob.gelu);
+  h->epoch = 0;
+
+  Params& P = h->params;
+  std::memset(&P, 0, sizeof(P));
+  const uint32_t bn = static_cast<uint32_t>(plan.tile_n);
+  const int dt = prob.dtype;
+  const bool sw = plan.swap_ab != 0;
+  // Up:   normal A = X [M,K] (128-row boxes), B = W1 [H,K] (bn-row boxes); swap exchanges them.
+  // Down: normal A = hidden [M,H], B = W2 [N,H]; swap exchanges them.
+  if (!sw) {
+    rc = encode_2d(&P.tm_a_up, b->x, dt, prob.k, prob.m, b->ldx, 64, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_up, b->w1, dt, prob.k, prob.h, b->ldw1, 64, bn);
+    if (!rc) rc = encode_2d(&P.tm_a_dn, b->hidden, dt, prob.h, prob.m, b->ldh, 64, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_dn, b->w2, dt, prob.h, prob.n, b->ldw2, 64, bn);
+    if (!rc) rc = encode_2d(&P.tm_st_hid, b->hidden, dt, prob.h, prob.m, b->ldh, 64, ffnb200::kStoreRows);
+    if (!rc) rc = encode_2d(&P.tm_st_y, b->y, dt, prob.n, prob.m, b->ldy, 64, ffnb200::kStoreRows);
+  } else {
+    rc = encode_2d(&P.tm_a_up, b->w1, dt, prob.k, prob.h, b->ldw1, 64, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_up, b->x, dt, prob.k, prob.m, b->ldx, 64, bn);
+    if (!rc) rc = encode_2d(&P.tm_a_dn, b->w2, dt, prob.h, prob.n, b->ldw2, 64, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_dn, b->hidden, dt, prob.h, prob.m, b->ldh, 64, bn);
+  }
+  if (rc) {
+    delete h;
+    return rc;
+  }
+  P.hidden = b->hidden;
+  P.y = b->y;
+  P.ldh = b->ldh;
+  P.ldy = b->ldy;
+  P.ws = b->workspace;
+  P.counters = b->counters;
+  P.flags = b->flags;
+  P.status = b->status;
+  auto to_sched = [](const ffn_b200_phase_plan& pp) {
+    PhaseSched s;
+    s.tiles_r = pp.tiles_r; s.tiles_q = pp.tiles_q; s.T = pp.tiles; s.L = pp.k_blocks;
+    s.dp = pp.dp_tiles; s.sk = pp.sk_tiles; s.q = pp.sk_iters; s.rem = pp.sk_rem; s.group = pp.group;
+    return s;
+  };
+  P.up = to_sched(plan.up);
+  P.dn = to_sched(plan.down);
+  P.M = static_cast<int>(prob.m);
+  P.H = static_cast<int>(prob.h);
+  P.N = static_cast<int>(prob.n);
+  P.C = plan.block_num;
+  P.wait_limit_ns = 4000000000ull;
+  P.inject = 0;
+  // Readiness counters gain 4 * (up tiles per row block) per launch, flags 4 per launch.
+  const int64_t per_blk = 4ll * (sw ? plan.up.tiles_r : plan.up.tiles_q);
+  h->epoch_limit = static_cast<unsigned>(((int64_t(1) << 30) / (per_blk > 4 ? per_blk : 4)));
+
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur != device) cudaSetDevice(device);
+  const cudaError_t e =
+      cudaFuncSetAttribute(h->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem_bytes));
+  if (cur != device) cudaSetDevice(cur);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    delete h;
+    return FFN_B200_ERR_CUDA;
+  }
+  *out = h;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_reset(ffn_b200_handle* h, void* stream) {
+  if (!h) return FFN_B200_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const ffn_b200_buffers& b = h->buf;
+  if (cudaMemsetAsync(b.counters, 0, sizeof(uint32_t) * h->plan.counter_words, st) != cudaSuccess ||
+      cudaMemsetAsync(b.flags, 0, sizeof(uint32_t) * h->plan.flag_words, st) != cudaSuccess ||
+      cudaMemsetAsync(b.status, 0, sizeof(int32_t) * h->plan.status_words, st) != cudaSuccess) {
+    cudaGetLastError();
+    return FFN_B200_ERR_CUDA;
+  }
+  h->epoch = 0;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_run(ffn_b200_handle* h, void* stream) {
+  if (!h) return FFN_B200_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (h->epoch + 1 >= h->epoch_limit) {
+    const int rc = ffn_b200_reset(h, stream);
+    if (rc) return rc;
+  }
+  h->epoch += 1;
+  h->params.epoch = h->epoch;
+
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(static_cast<unsigned>(h->plan.block_num), 1, 1);
+  cfg.blockDim = dim3(ffnb200::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(h->plan.smem_bytes);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, h->kernel, h->params);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    h->epoch -= 1;
+    return FFN_B200_ERR_CUDA;
+  }
+  return FFN_B200_OK;
+}
+
+int ffn_b200_rebind_io(ffn_b200_handle* h, const void* x, void* y) {
+  if (!h || !x || !y) return FFN_B200_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(y)) return FFN_B200_ERR_ALIGNMENT;
+  const ffn_b200_problem& pr = h->prob;
+  const int dt = pr.dtype;
+  const uint32_t bn = static_cast<uint32_t>(h->plan.tile_n);
+  Params P = h->params;
+  int rc;
+  if (!h->plan.swap_ab) {
+    rc = encode_2d(&P.tm_a_up, x, dt, pr.k, pr.m, h->buf.ldx, 64, 128);
+    if (!rc) rc = encode_2d(&P.tm_st_y, y, dt, pr.n, pr.m, h->buf.ldy, 64, ffnb200::kStoreRows);
+  } else {
+    rc = encode_2d(&P.tm_b_up, x, dt, pr.k, pr.m, h->buf.ldx, 64, bn);
+  }
+  if (rc) return rc;
+  P.y = y;
+  h->params = P;
+  h->buf.x = x;
+  h->buf.y = y;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_set_wait_limit(ffn_b200_handle* h, uint64_t ns) {
+  if (!h || ns == 0) return FFN_B200_ERR_INVALID;
+  h->params.wait_limit_ns = ns;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_set_fault_injection(ffn_b200_handle* h, int mode) {
+  if (!h || mode < 0 || mode > 1) return FFN_B200_ERR_INVALID;
+  h->params.inject = mode;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_get_plan(const ffn_b200_handle* h, ffn_b200_plan* plan) {
+  if (!h || !plan) return FFN_B200_ERR_INVALID;
+  *plan = h->plan;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_destroy(ffn_b200_handle* h) {
+  delete h;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_launch(const ffn_b200_problem* pr, const ffn_b200_buffers* b, void* stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FFN_B200_ERR_CUDA;
+  ffn_b200_handle* h = nullptr;
+  int rc = ffn_b200_prepare(pr, b, dev, &h);
+  if (rc) return rc;
+  rc = ffn_b200_reset(h, stream);
+  if (!rc) rc = ffn_b200_run(h, stream);
+  ffn_b200_destroy(h);
+  return rc;
+}
+
+}  // extern "C"

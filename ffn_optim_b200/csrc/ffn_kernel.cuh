@@ -1,0 +1,713 @@
+// Fused FFN kernel for sm_100a:  hidden = GELU(X . W1^T) ;  Y = hidden . W2^T  -- one launch.
+//
+// Replaces the two Ascend kernels of the reference (ops/kernel/ffn.py:55-585 "basic" and
+// ops/kernel/ffn.py:588-1423 "streamk").  Same arithmetic contract: fp16/bf16 operands,
+// fp32 accumulation, GELU in fp32 rounded once to the input dtype for the hidden tensor,
+// down-projection accumulated in fp32 and rounded once to the input dtype.
+//
+// Design (one persistent CTA per SM, 6 warps, warp-specialised):
+//   warp 0      TMA producer: 128B-swizzled A/B tiles into an S-stage shared-memory ring.
+//   warp 1      MMA issuer: tcgen05.mma (kind::f16, cta_group::1, M=128) into one of two
+//               TMEM accumulators; owns the TMEM allocation.
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> (Stream-K fixup) -> GELU / cast ->
+//               swizzled shared staging -> TMA store (or direct stores in swap mode).
+//
+// Work list of each CTA (static, identical for all three roles):
+//   up DP tiles, up Stream-K parts, down DP tiles, down Stream-K parts.
+// A down tile may start only when every up tile of its hidden row block has been stored:
+// the reference's global AIC/AIV rendezvous (ops/kernel/ffn.py:373-376, 582-585) becomes a
+// per-row-block readiness counter (release/acquire at GPU scope, bounded spin).  Counters
+// grow monotonically with the launch epoch, so they are never cleared between launches.
+//
+// Stream-K (reference ops/kernel/ffn.py:642-665 split, 1240-1422 fixup): the T mod C tail
+// tiles of a phase have their k-blocks split evenly over all C CTAs.  The CTA that owns a
+// tile's k = 0 block keeps its partial in TMEM, waits for the other contributors' fp32
+// partials and adds them in ascending CTA order (the reference sums in ascending core
+// order), then runs the normal epilogue.  The reduction order is fixed, so results are
+// deterministic run to run.
+//
+// "Swap" mode (M <= 64, decode): the weight rows become the 128-row MMA operand and the
+// tokens the MMA N dimension (16 or 64), so the kernel streams weights from HBM on all SMs.
+//
+// Every wait is bounded by a wall-clock limit (globaltimer); on expiry the kernel records
+// an error in status[], raises a CTA-local abort flag, drains its in-flight copies, frees
+// TMEM and returns.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace ffnb200 {
+
+constexpr int kBM = 128;          // MMA M (rows of the A operand per tile)
+constexpr int kBK = 64;           // K per pipeline stage = one 128-byte swizzle atom of 16-bit data
+constexpr int kThreads = 192;     // 6 warps
+constexpr int kEpiThreads = 128;  // warps 2..5
+constexpr int kABytes = kBM * kBK * 2;
+constexpr int kStoreRows = 32;    // rows per epilogue warp (one TMEM sub-partition)
+constexpr int kStageBufBytes = kStoreRows * 128;  // 32 rows x 64 x 16-bit, 128B-swizzled
+
+enum : int { kRoleFull = 0, kRoleOwner = 1, kRoleContrib = 2 };
+
+struct PhaseSched {
+  int tiles_r, tiles_q, T, L;  // tile grid, tiles, k-blocks per tile
+  int dp, sk, q, rem;          // data-parallel tiles, Stream-K tiles, k-blocks per CTA (+1 if c < rem)
+  int group;                   // raster group height in tile rows
+};
+
+struct Params {
+  CUtensorMap tm_a_up;   // up A operand  (X rows, or W1 rows in swap mode)
+  CUtensorMap tm_b_up;   // up B operand  (W1 rows, or X rows in swap mode)
+  CUtensorMap tm_a_dn;   // down A operand (hidden rows, or W2 rows in swap mode)
+  CUtensorMap tm_b_dn;   // down B operand (W2 rows, or hidden rows in swap mode)
+  CUtensorMap tm_st_hid; // hidden store map (normal mode)
+  CUtensorMap tm_st_y;   // Y store map (normal mode)
+  void* hidden;
+  void* y;
+  long long ldh, ldy;    // pitches in elements
+  float* ws;             // [2][C][kBM][BN] fp32 partials
+  unsigned* counters;    // readiness per token block
+  unsigned* flags;       // [2][C] partial-ready epochs
+  int* status;           // [0] code, [1] CTA, [2] aux
+  PhaseSched up, dn;
+  int M, H, N;
+  int C;
+  unsigned epoch;
+  unsigned long long wait_limit_ns;
+  int inject;
+};
+
+// ------------------------------------------------------------------------------------------
+// PTX wrappers
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+// TMA tiled load into this CTA's shared memory (no multicast), completion on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, both K-major, fp32 accumulate.
+__device__ __forceinline__ void umma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+      ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrive on an mbarrier once every tcgen05 op issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns; the wait is in the same asm block so the
+// outputs are never consumed before the load has landed.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major tile of 128-byte rows, 128B swizzle, 8-row
+// swizzle atoms 1024 B apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+// Instruction descriptor for kind::f16: D fp32, A/B fp16 or bf16, both K-major, M=128.
+template <bool BF16, int N>
+__host__ __device__ constexpr uint32_t make_idesc() {
+  return (1u << 4) | ((BF16 ? 1u : 0u) << 7) | ((BF16 ? 1u : 0u) << 10) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+// ------------------------------------------------------------------------------------------
+// Epilogue arithmetic
+// ------------------------------------------------------------------------------------------
+// The reference kernel's GELU: 0.5 z (1 + erf~(clip(z/sqrt2, +-3.92))), erf~ = t P(t^2) / Q(t^2)
+// with degree-5 P and Q.  Coefficients as in ops/kernel/ffn.py:556-566 and
+// validation/reference.py:5-13 (the reference's own published approximation).
+__device__ __forceinline__ float gelu_rational(float z) {
+  float t = fminf(fmaxf(z * 0.70710678118654752f, -3.92f), 3.92f);
+  float t2 = t * t;
+  float p = fmaf(t2, 0.053443748819f, 7.5517016694f);
+  p = fmaf(p, t2, 101.62808918f);
+  p = fmaf(p, t2, 1393.8061484f);
+  p = fmaf(p, t2, 5063.7915060f);
+  p = fmaf(p, t2, 29639.384698f);
+  p *= t;
+  float q = t2 + 31.212858877f;
+  q = fmaf(q, t2, 398.56963806f);
+  q = fmaf(q, t2, 3023.1248150f);
+  q = fmaf(q, t2, 13243.365831f);
+  q = fmaf(q, t2, 26267.224157f);
+  return 0.5f * z * (1.0f + __fdividef(p, q));
+}
+__device__ __forceinline__ float gelu_erf(float z) {
+  return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f));
+}
+template <int GELU>
+__device__ __forceinline__ float gelu(float z) {
+  if constexpr (GELU == 0) return gelu_rational(z);
+  else return gelu_erf(z);
+}
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+template <bool BF16>
+__device__ __forceinline__ uint16_t cvt1(float a) {
+  if constexpr (BF16) {
+    __nv_bfloat16 h = __float2bfloat16_rn(a);
+    return *reinterpret_cast<uint16_t*>(&h);
+  } else {
+    __half h = __float2half_rn(a);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Schedule
+// ------------------------------------------------------------------------------------------
+struct Unit {
+  int phase;     // 0 up, 1 down
+  int tile;      // raster index in [0, T)
+  int kb0, kb1;  // k-block range
+  int role;      // kRoleFull / kRoleOwner / kRoleContrib
+  int c_first, c_last;  // contributors whose partials an owner adds (ascending)
+};
+
+__device__ __forceinline__ int sk_start(const PhaseSched& s, int c) { return c * s.q + min(c, s.rem); }
+__device__ __forceinline__ int sk_cta_of(const PhaseSched& s, int i) {
+  const int big = s.rem * (s.q + 1);
+  if (i < big) return i / (s.q + 1);
+  return s.rem + (i - big) / s.q;
+}
+// Grouped raster: within a group of `group` tile rows, walk rows fastest then columns.
+__device__ __forceinline__ void tile_coords(const PhaseSched& s, int t, int& tr, int& tq) {
+  const int per_group = s.group * s.tiles_q;
+  const int g = t / per_group;
+  const int rem = t - g * per_group;
+  const int r0 = g * s.group;
+  const int gs = min(s.group, s.tiles_r - r0);
+  tr = r0 + rem % gs;
+  tq = rem / gs;
+}
+__device__ __forceinline__ bool get_unit(const Params& p, int c, int idx, Unit& u) {
+#pragma unroll 1
+  for (int ph = 0; ph < 2; ++ph) {
+    const PhaseSched& s = ph ? p.dn : p.up;
+    const int n_dp = c < s.dp ? (s.dp - c + p.C - 1) / p.C : 0;
+    if (idx < n_dp) {
+      u.phase = ph; u.tile = c + idx * p.C; u.kb0 = 0; u.kb1 = s.L;
+      u.role = kRoleFull; u.c_first = 1; u.c_last = 0;
+      return true;
+    }
+    idx -= n_dp;
+    int n_sk = 0, st = 0, en = 0;
+    if (s.sk > 0) {
+      st = sk_start(s, c);
+      en = sk_start(s, c + 1);
+      if (en > st) n_sk = (en - 1) / s.L - st / s.L + 1;
+    }
+    if (idx < n_sk) {
+      const int trel = st / s.L + idx;
+      const int tb = trel * s.L, te = tb + s.L;
+      const int a = max(st, tb), b = min(en, te);
+      u.phase = ph; u.tile = s.dp + trel; u.kb0 = a - tb; u.kb1 = b - tb;
+      if (a == tb) {
+        u.role = kRoleOwner; u.c_first = c + 1; u.c_last = sk_cta_of(s, te - 1);
+      } else {
+        u.role = kRoleContrib; u.c_first = 1; u.c_last = 0;
+      }
+      return true;
+    }
+    idx -= n_sk;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void report(const Params& p, int code, int aux) {
+  if (atomicCAS(p.status, 0, code) == 0) {
+    p.status[1] = static_cast<int>(blockIdx.x);
+    p.status[2] = aux;
+  }
+}
+
+// Bounded mbarrier wait.  Returns false when the CTA aborts (timeout here or elsewhere).
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                         const Params& p, int aux) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  uint32_t n = 0;
+#pragma unroll 1
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++n & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (gtimer() - t0 > p.wait_limit_ns) {
+        report(p, 1, aux);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+// Bounded wait until *word >= target (wrapping compare).  Acquire at GPU scope.
+__device__ __forceinline__ bool wait_word_ge(const unsigned* word, unsigned target, volatile int* abort_flag,
+                                             const Params& p, int code, int aux) {
+  if (static_cast<int>(ld_acquire(word) - target) >= 0) return true;
+  const uint64_t t0 = gtimer();
+#pragma unroll 1
+  while (true) {
+    __nanosleep(64);
+    if (static_cast<int>(ld_acquire(word) - target) >= 0) return true;
+    if (*abort_flag) return false;
+    if (gtimer() - t0 > p.wait_limit_ns) {
+      report(p, code, aux);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// The kernel
+// ------------------------------------------------------------------------------------------
+template <int BN, int STAGES, bool SWAP>
+struct Layout {
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiBytes = SWAP ? 0 : 4 * 2 * kStageBufBytes;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmem = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiBytes + kBarBytes;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static_assert((kBBytes % 1024) == 0, "B tile must be whole swizzle atoms");
+  static_assert((2 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");
+};
+
+template <int BN, int STAGES, bool SWAP, bool BF16, int GELU>
+__global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_constant__ Params p) {
+  using LY = Layout<BN, STAGES, SWAP>;
+  constexpr uint32_t kIdesc = make_idesc<BF16, BN>();
+  static_assert(SWAP || (BN % 64) == 0, "normal mode stores 64-column chunks");
+  static_assert(!SWAP || (BN % 16) == 0, "swap mode loads 16-column chunks");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sA = base;
+  const uint32_t sB = sA + STAGES * kABytes;
+  const uint32_t sE = sB + STAGES * LY::kBBytes;
+  const uint32_t sBar = sE + LY::kEpiBytes;
+  auto full_bar = [&](int s) { return sBar + 8u * s; };
+  auto empty_bar = [&](int s) { return sBar + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return sBar + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return sBar + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = sBar + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (sBar - base) + 8 * (2 * STAGES + 5));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+#pragma unroll 1
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), kEpiThreads);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_async_shared();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tm_a_up); prefetch_tmap(&p.tm_b_up);
+    prefetch_tmap(&p.tm_a_dn); prefetch_tmap(&p.tm_b_dn);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), LY::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      int ready_blk = -1;
+      const unsigned per_blk = 4u * static_cast<unsigned>(SWAP ? p.up.tiles_r : p.up.tiles_q);
+      const unsigned target = p.epoch * per_blk + (p.inject ? 1u : 0u);
+      bool ok = true;
+#pragma unroll 1
+      for (int idx = 0; ok; ++idx) {
+        Unit u;
+        if (!get_unit(p, cta, idx, u)) break;
+        const PhaseSched& s = u.phase ? p.dn : p.up;
+        int tr, tq;
+        tile_coords(s, u.tile, tr, tq);
+        const CUtensorMap* ta = u.phase ? &p.tm_a_dn : &p.tm_a_up;
+        const CUtensorMap* tb = u.phase ? &p.tm_b_dn : &p.tm_b_up;
+        if (u.phase == 1) {
+          const int blk = SWAP ? tq : tr;
+          if (blk != ready_blk) {
+            if (!wait_word_ge(p.counters + blk, target, abort_flag, p, 2, blk)) { ok = false; break; }
+            fence_async_global();
+            ready_blk = blk;
+          }
+        }
+#pragma unroll 1
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+          if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) { ok = false; break; }
+          mbar_expect_tx(full_bar(stage), LY::kStageBytes);
+          tma_load_2d(sA + stage * kABytes, ta, kb * kBK, tr * kBM, full_bar(stage));
+          tma_load_2d(sB + stage * LY::kBBytes, tb, kb * kBK, tq * BN, full_bar(stage));
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: every issued load must land before the CTA may exit.
+      const long long first = issued > STAGES ? issued - STAGES : 0;
+#pragma unroll 1
+      for (long long i = first; i < issued; ++i) {
+        const int s = static_cast<int>(i % STAGES);
+        const uint32_t par = static_cast<uint32_t>((i / STAGES) & 1);
+        const uint64_t t0 = gtimer();
+        while (!mbar_try_wait(full_bar(s), par)) {
+          if (gtimer() - t0 > p.wait_limit_ns) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+#pragma unroll 1
+      for (int idx = 0; ok; ++idx) {
+        Unit u;
+        if (!get_unit(p, cta, idx, u)) break;
+        if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, p, 200 + acc)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+          if (!wait_bar(full_bar(stage), phase, abort_flag, p, 300 + stage)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(sA + stage * kABytes);
+          const uint64_t db = sw128_desc(sB + stage * LY::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes along K inside the 128-byte swizzle atom = +2 in the 16-byte address field
+            umma_f16(d, da + 2 * k, db + 2 * k, kIdesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      // Drain: all issued MMAs complete before TMEM is released.
+      umma_commit(drain_bar);
+      const uint64_t t0 = gtimer();
+      while (!mbar_try_wait(drain_bar, 0)) {
+        if (gtimer() - t0 > p.wait_limit_ns) break;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int ew = warp - 2;            // staging-buffer owner index
+    const int sub = warp & 3;           // TMEM lane sub-partition this warp may access
+    const int row = sub * 32 + lane;    // row inside the 128-row tile
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int sbuf = 0;
+#pragma unroll 1
+    for (int idx = 0;; ++idx) {
+      Unit u;
+      if (!get_unit(p, cta, idx, u)) break;
+      const PhaseSched& s = u.phase ? p.dn : p.up;
+      int tr, tq;
+      tile_coords(s, u.tile, tr, tq);
+      int ok = 1;
+      if (lane == 0) ok = wait_bar(tfull_bar(acc), acc_phase, abort_flag, p, 400 + acc) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      // Stream-K owner: wait for every contributor's partial of this tile.
+      if (u.role == kRoleOwner && u.c_first <= u.c_last) {
+        if (lane == 0) {
+          for (int c2 = u.c_first; c2 <= u.c_last && ok; ++c2)
+            ok = wait_word_ge(p.flags + u.phase * p.C + c2, 4u * p.epoch, abort_flag, p, 3, c2) ? 1 : 0;
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        for (int c2 = u.c_first; c2 <= u.c_last; ++c2) (void)ld_acquire(p.flags + u.phase * p.C + c2);
+      }
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      float* ws_own = p.ws + (static_cast<size_t>(u.phase * p.C + cta) * kBM + row) * BN;
+
+      if constexpr (!SWAP) {
+        // Normal mode: tile rows are tokens, columns are features (H for up, N for down).
+        const CUtensorMap* tms = u.phase ? &p.tm_st_y : &p.tm_st_hid;
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 64; ++ch) {
+          float v[64];
+          tmem_ld32(tbase + ch * 64, v);
+          tmem_ld32(tbase + ch * 64 + 32, v + 32);
+          if (u.role == kRoleContrib) {
+            float4* dst = reinterpret_cast<float4*>(ws_own + ch * 64);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            continue;
+          }
+          if (u.role == kRoleOwner) {
+#pragma unroll 1
+            for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  p.ws + (static_cast<size_t>(u.phase * p.C + c2) * kBM + row) * BN + ch * 64);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float4 t = __ldcg(src + j);
+                v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+              }
+            }
+          }
+          if (u.phase == 0) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = gelu<GELU>(v[j]);
+          }
+          uint32_t pk[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) pk[j] = pack2<BF16>(v[2 * j], v[2 * j + 1]);
+          // Staging buffer (32 rows x 128 B, 128B-swizzled) owned by this warp.
+          const uint32_t sb = sE + static_cast<uint32_t>((ew * 2 + sbuf) * kStageBufBytes);
+          if (lane == 0) bulk_wait_read1();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t addr = sb + lane * 128 + ((j ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * j]),
+                         "r"(pk[4 * j + 1]), "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
+                         : "memory");
+          }
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(tms, sb, tq * BN + ch * 64, tr * kBM + sub * 32);
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        }
+      } else {
+        // Swap mode: tile rows are features (H for up, N for down), columns are tokens.
+        const int feat = tr * kBM + row;
+        const int F = u.phase ? p.N : p.H;
+        uint16_t* out = reinterpret_cast<uint16_t*>(u.phase ? p.y : p.hidden);
+        const long long ld = u.phase ? p.ldy : p.ldh;
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 16; ++ch) {
+          float v[16];
+          tmem_ld16(tbase + ch * 16, v);
+          if (u.role == kRoleContrib) {
+            float4* dst = reinterpret_cast<float4*>(ws_own + ch * 16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            continue;
+          }
+          if (u.role == kRoleOwner) {
+#pragma unroll 1
+            for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  p.ws + (static_cast<size_t>(u.phase * p.C + c2) * kBM + row) * BN + ch * 16);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 t = __ldcg(src + j);
+                v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+              }
+            }
+          }
+          if (feat < F) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = tq * BN + ch * 16 + j;
+              if (m < p.M) {
+                const float val = u.phase == 0 ? gelu<GELU>(v[j]) : v[j];
+                out[static_cast<long long>(m) * ld + feat] = cvt1<BF16>(val);
+              }
+            }
+          }
+        }
+      }
+      // Release the TMEM accumulator to the MMA warp.
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+
+      if (u.role == kRoleContrib) {
+        // Publish this warp's 32 rows of the partial: one release per warp, so the owner
+        // waits for 4 signals per launch and no CTA-wide barrier is involved.
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) red_release_add(p.flags + u.phase * p.C + cta, 1u);
+      } else if (u.phase == 0) {
+        // Hidden tile stored: signal the row block (one signal per warp).
+        const int blk = SWAP ? tq : tr;
+        if constexpr (!SWAP) {
+          if (lane == 0) {
+            bulk_wait_all();
+            fence_async_global();
+            red_release_add(p.counters + blk, 1u);
+          }
+          __syncwarp();
+        } else {
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) red_release_add(p.counters + blk, 1u);
+        }
+      }
+    }
+    if constexpr (!SWAP) {
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, LY::kTmemCols);
+}
+
+}  // namespace ffnb200

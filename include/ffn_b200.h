@@ -1,0 +1,172 @@
+/*
+ * ffn_b200.h -- C ABI of the B200 fused feed-forward operator
+ *
+ *     Y = GELU(X . W1^T) . W2^T      (fp16 or bf16, no bias, inference only)
+ *
+ * X is [M, K] row-major, W1 is [H, K] (torch Linear layout), W2 is [N, H], Y is [M, N].
+ * All pointers are device pointers owned by the caller; the library allocates no device
+ * memory and never synchronises the stream it is given.
+ *
+ * Each entry point replaces one piece of the reference implementation (hxtsg/ffn_optim):
+ *
+ *   ffn_b200_make_plan  <- ops/host/tiling.py:58-74 (make_plan) together with the
+ *                          Selection rules of ops/host/dispatch.py:42-66
+ *   ffn_b200_prepare    <- ops/api.py:48-89 (prepare_ffn: device checks, block_num limit,
+ *                          compile_kernel of ops/host/dispatch.py:97-116)
+ *   ffn_b200_run        <- ops/api.py:37-45 (PreparedFFN.run -> artifact(...) launch, the
+ *                          single host->device boundary of the reference)
+ *   ffn_b200_launch     <- ops/api.py:92-94 (ffn: prepare + run in one call)
+ *
+ * Return codes are FFN_B200_OK (0) or one of the ffn_b200_status values below; the Python
+ * host layer maps them onto the reference's exception types (ValueError, NotApplicable,
+ * DependencyUnavailable, KernelCompilationError, RuntimeError).
+ */
+#ifndef FFN_B200_H
+#define FFN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFN_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FFN_B200_EXPORT __attribute__((visibility("default")))
+#else
+#define FFN_B200_EXPORT
+#endif
+
+typedef enum {
+  FFN_B200_OK = 0,
+  FFN_B200_ERR_INVALID = 1,        /* bad shape, pointer, pitch or enum (reference: ValueError) */
+  FFN_B200_ERR_NOT_APPLICABLE = 2, /* streamk without a tail wave (reference: NotApplicable) */
+  FFN_B200_ERR_UNAVAILABLE = 3,    /* full_load_a / full_load_b (reference: DependencyUnavailable) */
+  FFN_B200_ERR_DEVICE = 4,         /* not an sm_100 device or block_num > SM count */
+  FFN_B200_ERR_CUDA = 5,           /* a CUDA runtime / driver call failed */
+  FFN_B200_ERR_ALIGNMENT = 6,      /* base not 16-byte aligned or pitch not a multiple of 8 elements */
+  FFN_B200_ERR_TOO_LARGE = 7       /* tile count does not fit one launch */
+} ffn_b200_status;
+
+typedef enum { FFN_B200_F16 = 0, FFN_B200_BF16 = 1 } ffn_b200_dtype;
+
+/* Index into the reference's DOWN_IMPLS tuple (ops/host/dispatch.py:15). */
+typedef enum {
+  FFN_B200_DOWN_BASIC = 0,
+  FFN_B200_DOWN_FULL_LOAD_A = 1,
+  FFN_B200_DOWN_FULL_LOAD_B = 2,
+  FFN_B200_DOWN_STREAMK = 3
+} ffn_b200_down_impl;
+
+/* GELU form used in the up-projection epilogue.  RATIONAL is the reference kernel's
+ * clipped rational erf (ops/kernel/ffn.py:548-572, validation/reference.py:5-13);
+ * ERF calls CUDA's erff. */
+typedef enum { FFN_B200_GELU_RATIONAL = 0, FFN_B200_GELU_ERF = 1 } ffn_b200_gelu;
+
+/* Device-side error codes written to status[0] by the kernel (0 = no error). */
+typedef enum {
+  FFN_B200_KERNEL_OK = 0,
+  FFN_B200_KERNEL_PIPE_TIMEOUT = 1, /* an on-chip pipeline wait ran past the wait limit */
+  FFN_B200_KERNEL_DEP_TIMEOUT = 2,  /* a down tile waited too long for its hidden rows */
+  FFN_B200_KERNEL_SK_TIMEOUT = 3    /* a Stream-K owner waited too long for a partial */
+} ffn_b200_kernel_error;
+
+typedef struct {
+  int64_t m, k, h, n;  /* M = prod(leading dims of X) */
+  int32_t dtype;       /* ffn_b200_dtype */
+  int32_t down_impl;   /* ffn_b200_down_impl */
+  int32_t gelu;        /* ffn_b200_gelu */
+  int32_t block_num;   /* persistent CTA count; 0 = one per SM */
+  int32_t sm_count;    /* SMs of the target device; 0 = query the current device */
+} ffn_b200_problem;
+
+/* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
+ * rows/cols are the tile grid of the MMA's A and B operands; k_blocks is the number of
+ * 64-wide K steps per tile.  dp_tiles are computed whole by one CTA; the sk_tiles tail
+ * is split along K over all CTAs (Stream-K), sk_iters (+1 for the first sk_rem CTAs)
+ * K steps per CTA. */
+typedef struct {
+  int32_t tiles_r, tiles_q, tiles, k_blocks;
+  int32_t dp_tiles, sk_tiles, sk_iters, sk_rem;
+  int32_t group;
+} ffn_b200_phase_plan;
+
+typedef struct {
+  int32_t variant;       /* kernel instantiation id */
+  int32_t swap_ab;       /* 1: weights are the MMA's M operand and tokens its N (small M) */
+  int32_t tile_m, tile_n, tile_k, stages;
+  int32_t block_num;
+  int32_t tmem_cols;
+  int64_t smem_bytes;
+  ffn_b200_phase_plan up, down;
+  int64_t workspace_floats; /* fp32 Stream-K partials: 2 phases x block_num x tile_m x tile_n */
+  int64_t counter_words;    /* u32 hidden-row-block readiness counters */
+  int64_t flag_words;       /* u32 Stream-K partial-ready flags: 2 x block_num */
+  int64_t status_words;     /* i32 status words */
+} ffn_b200_plan;
+
+/* Device buffers.  ld* are row pitches in elements; each must be a multiple of 8 and each
+ * base 16-byte aligned (TMA).  hidden is [M, ldh] scratch of the input dtype; y is the
+ * [M, ldy] output.  workspace/counters/flags/status are sized by ffn_b200_plan and must be
+ * zero-filled before the first run of a handle. */
+typedef struct {
+  const void* x;  int64_t ldx;
+  const void* w1; int64_t ldw1;
+  const void* w2; int64_t ldw2;
+  void* hidden;   int64_t ldh;
+  void* y;        int64_t ldy;
+  float* workspace;
+  uint32_t* counters;
+  uint32_t* flags;
+  int32_t* status;
+} ffn_b200_buffers;
+
+typedef struct ffn_b200_handle ffn_b200_handle;
+
+FFN_B200_EXPORT int ffn_b200_abi_version(void);
+FFN_B200_EXPORT const char* ffn_b200_strerror(int code);
+
+/* Number of SMs and compute capability of a device (no kernel launch). */
+FFN_B200_EXPORT int ffn_b200_device_info(int device, int* sm_count, int* cc_major, int* cc_minor);
+
+/* Host-only planning: tile shapes, Stream-K split and scratch sizes.  Needs no GPU when
+ * problem->sm_count > 0. */
+FFN_B200_EXPORT int ffn_b200_make_plan(const ffn_b200_problem* problem, ffn_b200_plan* plan);
+
+/* Validates device and buffers, encodes the TMA tensor maps and returns a handle that
+ * launches one fused kernel per ffn_b200_run.  The handle keeps a launch epoch so the
+ * readiness counters never need clearing between runs. */
+FFN_B200_EXPORT int ffn_b200_prepare(const ffn_b200_problem* problem, const ffn_b200_buffers* buffers,
+                     int device, ffn_b200_handle** handle);
+
+/* One asynchronous launch on `stream` (a cudaStream_t).  Runs of one handle must be
+ * serialised on one stream. */
+FFN_B200_EXPORT int ffn_b200_run(ffn_b200_handle* handle, void* stream);
+
+/* Re-points X and Y of a prepared handle (same shapes and pitches) without re-planning. */
+FFN_B200_EXPORT int ffn_b200_rebind_io(ffn_b200_handle* handle, const void* x, void* y);
+
+/* Clears counters, flags and status on `stream` and restarts the epoch; call after a run
+ * reported a kernel error. */
+FFN_B200_EXPORT int ffn_b200_reset(ffn_b200_handle* handle, void* stream);
+
+/* Upper bound, in nanoseconds, of every wait inside the kernel (default 4 s). */
+FFN_B200_EXPORT int ffn_b200_set_wait_limit(ffn_b200_handle* handle, uint64_t nanoseconds);
+
+/* Test hook: 1 makes every down tile wait for one readiness signal too many, so the
+ * bounded wait runs out and the kernel reports FFN_B200_KERNEL_DEP_TIMEOUT. */
+FFN_B200_EXPORT int ffn_b200_set_fault_injection(ffn_b200_handle* handle, int mode);
+
+FFN_B200_EXPORT int ffn_b200_get_plan(const ffn_b200_handle* handle, ffn_b200_plan* plan);
+FFN_B200_EXPORT int ffn_b200_destroy(ffn_b200_handle* handle);
+
+/* One-shot: prepare, clear the scratch words, run once, release the handle. */
+FFN_B200_EXPORT int ffn_b200_launch(const ffn_b200_problem* problem, const ffn_b200_buffers* buffers,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FFN_B200_H */

@@ -1,0 +1,122 @@
+"""CPU oracle of the fused FFN -- TEST INFRASTRUCTURE ONLY.
+
+This module is the checker, never the product: only ``tests/``, ``__graft_entry__.smoke()``
+and ``bench.py``'s CPU-baseline / reference leg may import it.  The product path
+(``ffn_optim_b200``) never imports it and has no CPU fallback.
+
+It restates, in numpy (float32 BLAS + explicit rounding), the reference's torch golden path
+``validation/reference.py`` of hxtsg/ffn_optim:
+
+  * :func:`gelu_rational`  <- validation/reference.py:5-13 (the kernel's clipped rational erf;
+    same coefficients as ops/kernel/ffn.py:556-566)
+  * :func:`gelu_erf`       <- torch.nn.functional.gelu(approximate='none') as called at
+    validation/reference.py:20  (0.5 z (1 + erf(z / sqrt 2)), scipy's erf)
+  * :func:`ffn`            <- validation/reference.py:16-23 (fp32 X.W1^T -> GELU -> optional
+    hidden rounding to the input dtype (staged) -> fp32 .W2^T -> round to the input dtype)
+  * :func:`round_to`       <- the ``.to(x.dtype)`` casts: IEEE round-to-nearest-even to fp16 /
+    bf16
+
+Pinning: ``tests/golden/`` holds outputs of the reference's own ``ffn_torch`` (imported from
+the reference checkout by ``tests/golden/make_golden.py``) on the seeded inputs of each case;
+``tests/test_oracle.py`` checks this restatement against them (at most one unit in the last
+place of the output dtype apart, the difference between two fp32 BLAS summation orders).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+SQRT1_2 = np.float32(0.70710678118654752)
+
+_P = (0.053443748819, 7.5517016694, 101.62808918, 1393.8061484, 5063.7915060, 29639.384698)
+_Q = (31.212858877, 398.56963806, 3023.1248150, 13243.365831, 26267.224157)
+
+
+def gelu_rational(z):
+    """Clipped rational-erf GELU in float32 (validation/reference.py:5-13).
+
+    Evaluated with the same operation order as the reference (torch applies the Python
+    float constants to float32 tensors as float32 scalars): t = clip(z/sqrt2, +-3.92),
+    p = t * P(t^2), q = Q(t^2), result 0.5 z (1 + p / q).
+    """
+    z = np.asarray(z, dtype=np.float32)
+    f = np.float32
+    t = np.clip(z * SQRT1_2, f(-3.92), f(3.92))
+    t2 = t * t
+    p = t2 * f(_P[0]) + f(_P[1])
+    for c in _P[2:]:
+        p = p * t2 + f(c)
+    p = p * t
+    q = t2 + f(_Q[0])
+    for c in _Q[1:]:
+        q = q * t2 + f(c)
+    return f(0.5) * z * (f(1) + p / q)
+
+
+def gelu_erf(z):
+    """Exact-erf GELU in float32: 0.5 z (1 + erf(z / sqrt 2))."""
+    from scipy.special import erf
+
+    z = np.asarray(z, dtype=np.float32)
+    return (z * np.float32(0.5) * (np.float32(1) + erf(z * SQRT1_2).astype(np.float32))).astype(np.float32)
+
+
+def bf16_bits(a):
+    """float32 -> bfloat16 bit patterns, round to nearest even (NaN stays NaN)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    rounded = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)
+    nan = np.isnan(a)
+    out = rounded.astype(np.uint16)
+    if nan.any():
+        out[nan] = np.uint16(0x7FC0)
+    return out
+
+
+def bf16_to_f32(bits):
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def to_bits(a, dtype):
+    """float32 values -> uint16 bit patterns of ``dtype`` ('float16' | 'bfloat16')."""
+    if dtype == "bfloat16":
+        return bf16_bits(a)
+    if dtype == "float16":
+        return np.asarray(a, dtype=np.float32).astype(np.float16).view(np.uint16)
+    raise ValueError(dtype)
+
+
+def from_bits(bits, dtype):
+    """uint16 bit patterns of ``dtype`` -> float32 values."""
+    if dtype == "bfloat16":
+        return bf16_to_f32(bits)
+    if dtype == "float16":
+        return np.asarray(bits, dtype=np.uint16).view(np.float16).astype(np.float32)
+    raise ValueError(dtype)
+
+
+def round_to(a, dtype):
+    """Rounds float32 values to ``dtype`` and returns them as float32 (the ``.to(dtype)`` cast)."""
+    return from_bits(to_bits(a, dtype), dtype)
+
+
+def ffn(x, w1, w2, dtype, *, staged=False, rational=False):
+    """Oracle of validation/reference.py:16-23 on float32 arrays holding ``dtype`` values.
+
+    ``x`` is [..., K] (already restricted to the rows of interest), ``w1`` [H, K],
+    ``w2`` [N, H].  Returns the output's uint16 bit patterns, shape [..., N].
+    """
+    x = np.asarray(x, dtype=np.float32)
+    lead = x.shape[:-1]
+    z = x.reshape(-1, x.shape[-1]) @ np.asarray(w1, dtype=np.float32).T
+    hidden = gelu_rational(z) if rational else gelu_erf(z)
+    if staged:
+        hidden = round_to(hidden, dtype)
+    y = hidden @ np.asarray(w2, dtype=np.float32).T
+    return to_bits(y, dtype).reshape(*lead, w2.shape[0])
+
+
+def ulp_distance(a_bits, b_bits):
+    """Distance in representable steps between two uint16 arrays of the same 16-bit format."""
+    def key(b):
+        b = np.asarray(b, dtype=np.uint16).astype(np.int32)
+        return np.where(b & 0x8000, 0x8000 - (b & 0x7FFF), 0x8000 + b)
+    return np.abs(key(a_bits) - key(b_bits))

@@ -1,0 +1,34 @@
+"""Failure detection without a GPU fault: a readiness flag that nothing sets makes the
+kernel's bounded wait run out; the kernel reports the error in its status words, returns,
+and the context stays usable (a reset and the next run are correct)."""
+import numpy as np
+import pytest
+import torch
+
+from ffn_optim_b200 import prepare_ffn
+from ffn_optim_b200 import cases as C
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("case_id", ["cfg1_fp16", "cfg3_bf16"])
+def test_dependency_wait_times_out_and_recovers(case_id):
+    case = C.get_case(case_id)
+    x, w1, w2 = C.make_inputs(case, device="cuda")
+    prepared = prepare_ffn(x, w1, w2, down_impl="basic")
+    good = prepared.run().clone()
+    prepared.check()
+    prepared.set_wait_limit(0.2)
+    prepared.set_fault_injection(1)
+    prepared.run()
+    status = prepared.status()
+    assert status[0] == 2, status  # FFN_B200_KERNEL_DEP_TIMEOUT
+    with pytest.raises(RuntimeError, match="readiness wait timed out"):
+        prepared.check()  # also resets counters, flags and status
+    prepared.set_fault_injection(0)
+    prepared.set_wait_limit(2.0)
+    y = prepared.run()
+    prepared.check()
+    assert torch.equal(y, good)
+    torch.cuda.synchronize()
+    assert np.isfinite(y.float().cpu().numpy()).all()

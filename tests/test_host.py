@@ -1,0 +1,215 @@
+"""CPU tests of the host layer and the C ABI (no GPU): input contract, criterion, selection,
+planning, storage preparation, and that the library exports everything the header declares.
+
+Mirrors the reference's validation/test_ffn.py InputTests / MetricTests / CompositionTests
+(test_selection) where the behaviour is shared.
+"""
+import ctypes
+import re
+import subprocess
+import tempfile
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from ffn_optim_b200 import (DependencyUnavailable, NotApplicable, Selection, compare, ffn, make_plan,
+                            problem_from_shapes, validate_tensors)
+from ffn_optim_b200 import _lib
+from ffn_optim_b200 import cases as C
+from ffn_optim_b200.host.inputs import prepare_storage
+from oracle import ffn_oracle as O
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "ffn_b200.h"
+
+
+# ---------------------------------------------------------------- input contract
+def test_ranks_and_storage():
+    """Ranks 2-8 x fp16/bf16 with stride-2 inputs: storage holds the same rows and the
+    oracle on storage equals the oracle on the original tensors (reference test_ffn.py:31-48)."""
+    for dtype in (torch.float16, torch.bfloat16):
+        for rank in range(2, 9):
+            shape = (1,) * (rank - 2) + (3, 17)
+            x = torch.randn((*shape[:-1], 34)).to(dtype)[..., ::2]
+            w1 = torch.randn(19, 34).to(dtype)[:, ::2]
+            w2 = torch.randn(23, 38).to(dtype)[:, ::2]
+            p = validate_tensors(x, w1, w2)
+            plan = make_plan(p, sm_count=148)
+            x2d, a, b, hidden, out, ws, cnt, flg, st = prepare_storage(x, w1, w2, plan)
+            for t, rows in ((x2d, p.m), (a, p.h), (b, p.n), (hidden, p.m), (out, p.m)):
+                assert t.shape[0] == rows and t.stride(0) % 8 == 0 and t.stride(1) == 1
+            dt = p.dtype
+            f = lambda t: t.float().numpy()  # noqa: E731
+            got = O.ffn(f(x2d[:, :p.k]), f(a[:, :p.k]), f(b[:, :p.h]), dt, staged=True)
+            ref = O.ffn(f(x.reshape(p.m, p.k)), f(w1), f(w2), dt, staged=True)
+            assert np.array_equal(got, ref)
+            assert p.output_shape == (*shape[:-1], 23)
+            assert int(cnt.abs().sum()) == 0 and int(flg.abs().sum()) == 0 and int(st.abs().sum()) == 0
+
+
+def test_invalid_shapes():
+    for args in [([3], [4, 3], [3, 4]), ([0, 3], [4, 3], [3, 4]), ([2, 3], [4, 2], [3, 4]),
+                 ([1] * 9, [4, 1], [3, 4]), ([True, 3], [4, 3], [3, 4]), ([2, 65536], [4, 65536], [3, 4])]:
+        with pytest.raises(ValueError):
+            problem_from_shapes(*args)
+    for kwargs in ({"dtype": "float32"}, {"layout": "canonical"}):
+        with pytest.raises(ValueError):
+            problem_from_shapes([2, 3], [4, 3], [3, 4], **kwargs)
+
+
+def test_no_cpu_fallback():
+    with pytest.raises(ValueError, match="requires CUDA"):
+        ffn(torch.zeros(2, 3).half(), torch.zeros(4, 3).half(), torch.zeros(3, 4).half())
+
+
+def test_invalid_tensors():
+    x, a, b = torch.zeros(2, 3).half(), torch.zeros(4, 3).half(), torch.zeros(3, 4).half()
+    with pytest.raises(ValueError):
+        validate_tensors(x, a.float(), b)
+    with pytest.raises(ValueError):
+        validate_tensors(x.requires_grad_(), a, b)
+    with pytest.raises(TypeError):
+        validate_tensors(x.detach().numpy(), a, b)
+
+
+# ---------------------------------------------------------------- criterion
+def test_bad_results():
+    a = torch.ones(2, 3).half()
+    assert compare(a, a)["passed"] and compare(a, a, strict=True)["passed"]
+    for bad in (a.float(), a.T, a * float("nan"), a * float("inf"), a * 2):
+        assert not compare(bad, a)["passed"]
+
+
+def test_max_abs_bound_is_strict_only():
+    gold = torch.linspace(-1, 1, 1000).half()
+    out = gold.clone()
+    out[0] += 0.5  # one large error: mean_rel small, max_abs over 2e-2 * max|golden|
+    r = compare(out, gold)
+    assert r["passed"] and not r["max_abs_ok"] and not compare(out, gold, strict=True)["passed"]
+
+
+# ---------------------------------------------------------------- selection and planning
+def test_selection():
+    for kind in ("full_load_a", "full_load_b"):
+        with pytest.raises(DependencyUnavailable):
+            Selection(down_impl=kind).require_available()
+    with pytest.raises(ValueError):
+        Selection(up_impl="streamk")
+    with pytest.raises(ValueError):
+        Selection(down_impl="bogus")
+    p = problem_from_shapes([64, 128], [256, 128], [64, 256])
+    plan = make_plan(p, Selection(down_impl="streamk"), 8, sm_count=148)
+    assert plan.workspace_shape == (2 * 8 * 128, plan.kernel["tile_n"])
+    with pytest.raises(NotApplicable):
+        make_plan(p, Selection(down_impl="streamk"), 1, sm_count=148)
+    with pytest.raises(ValueError):
+        make_plan(p, Selection(), 0, sm_count=148)
+
+
+def _units(phase, C):
+    """Python model of the device work list: (cta, tile, kb0, kb1, role)."""
+    units = []
+    for c in range(C):
+        for t in range(c, phase["dp_tiles"], C):
+            units.append((c, t, 0, phase["k_blocks"], "full"))
+        if phase["sk_tiles"]:
+            q, r, L = phase["sk_iters"], phase["sk_rem"], phase["k_blocks"]
+            st, en = c * q + min(c, r), (c + 1) * q + min(c + 1, r)
+            i = st
+            while i < en:
+                t = i // L
+                e = min(en, (t + 1) * L)
+                units.append((c, phase["dp_tiles"] + t, i - t * L, e - t * L, "owner" if i == t * L else "contrib"))
+                i = e
+    return units
+
+
+@pytest.mark.parametrize("case_id", [c["case_id"] for c in C.load_cases()])
+def test_plan_covers_every_k_block_once(case_id):
+    case = C.get_case(case_id)
+    p = C.case_problem(case)
+    for down in ("basic", "streamk"):
+        try:
+            plan = make_plan(p, Selection(down_impl=down), sm_count=148)
+        except NotApplicable:
+            assert down == "streamk"
+            continue
+        k = plan.kernel
+        assert k["block_num"] == 148
+        if p.m <= 16:
+            assert k["swap_ab"] == 1 and k["tile_n"] == 16
+        elif p.m <= 64:
+            assert k["swap_ab"] == 1 and k["tile_n"] == 64
+        for name in ("up", "down"):
+            ph = k[name]
+            assert ph["tiles"] == ph["tiles_r"] * ph["tiles_q"]
+            cover = {}
+            owners = {}
+            for c, t, a, b, role in _units(ph, 148):
+                for kb in range(a, b):
+                    cover[(t, kb)] = cover.get((t, kb), 0) + 1
+                if role in ("full", "owner"):
+                    owners[t] = owners.get(t, 0) + 1
+            assert len(cover) == ph["tiles"] * ph["k_blocks"] and set(cover.values()) == {1}
+            assert len(owners) == ph["tiles"] and set(owners.values()) == {1}
+        if down == "basic":
+            assert k["down"]["sk_tiles"] == 0
+
+
+def test_baseline_variants():
+    want = {"cfg3_bf16": (1, 16), "cfg4_bf16": (0, 256), "cfg5_bf16": (0, 256), "cfg1_fp16": (0, 128),
+            "cfg2_bf16": (0, 128)}
+    for cid, (swap, bn) in want.items():
+        case = C.get_case(cid)
+        plan = make_plan(C.case_problem(case), Selection(down_impl=case["down_impl"]), sm_count=148)
+        assert (plan.kernel["swap_ab"], plan.kernel["tile_n"]) == (swap, bn), cid
+
+
+# ---------------------------------------------------------------- the C ABI
+def _declared():
+    text = HEADER.read_text()
+    return re.findall(r"FFN_B200_EXPORT\s+[\w\s\*]+?\b(ffn_b200_\w+)\s*\(", text)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = _declared()
+    assert len(names) >= 13
+    assert set(names) == set(_lib.EXPORTED)
+    for name in names:
+        assert hasattr(lib, name), name
+    assert lib.ffn_b200_abi_version() == 1
+    assert lib.ffn_b200_strerror(2).decode().startswith("Stream-K")
+
+
+def test_ctypes_structs_match_the_header():
+    src = f'''#include <stdio.h>
+#include <stddef.h>
+#include "{HEADER}"
+int main(void) {{
+  printf("%zu %zu %zu %zu\\n", sizeof(ffn_b200_problem), sizeof(ffn_b200_plan), sizeof(ffn_b200_buffers),
+         offsetof(ffn_b200_plan, workspace_floats));
+  return 0;
+}}'''
+    with tempfile.TemporaryDirectory() as d:
+        c, exe = Path(d) / "s.c", Path(d) / "s"
+        c.write_text(src)
+        subprocess.run(["gcc", "-o", str(exe), str(c)], check=True)
+        sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert sizes == [ctypes.sizeof(_lib.Problem), ctypes.sizeof(_lib.PlanInfo), ctypes.sizeof(_lib.Buffers),
+                     _lib.PlanInfo.workspace_floats.offset]
+
+
+def test_c_planner_rejects_bad_problems(lib):
+    info = _lib.PlanInfo()
+    for m, k, h, n, dt, down in [(0, 8, 8, 8, 1, 0), (8, 70000, 8, 8, 1, 0), (8, 8, 8, 8, 5, 0), (8, 8, 8, 8, 1, 9)]:
+        prob = _lib.Problem(m, k, h, n, dt, down, 0, 0, 148)
+        assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_INVALID
+    prob = _lib.Problem(64, 64, 64, 64, 1, 1, 0, 0, 148)
+    assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_UNAVAILABLE
+    # prepare without a usable device fails cleanly (no GPU in the CPU suite, or bad pointers)
+    bufs = _lib.Buffers()
+    h = ctypes.c_void_p()
+    prob = _lib.Problem(64, 64, 64, 64, 1, 0, 0, 0, 148)
+    assert lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), 0, ctypes.byref(h)) != 0

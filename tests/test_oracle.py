@@ -1,0 +1,96 @@
+"""Pins the CPU oracle (oracle/ffn_oracle.py) to the reference's own outputs.
+
+The fixtures in tests/golden/ were produced by the reference's validation/reference.py
+(ffn_torch, gelu_rational) on the seeded inputs of every case; see make_golden.py.
+"""
+import numpy as np
+import pytest
+
+from ffn_optim_b200 import cases as C
+from oracle import ffn_oracle as O
+
+GOLDEN = C.CASES_FILE.parents[2] / "tests" / "golden"
+CASE_IDS = [c["case_id"] for c in C.load_cases()]
+FAST = [c for c in CASE_IDS if not c.startswith(("cfg4", "cfg5"))]
+
+
+def _fixture(case_id):
+    return np.load(GOLDEN / f"{case_id}.npz")
+
+
+def test_gelu_rational_bit_exact_vs_reference():
+    g = np.load(GOLDEN / "gelu.npz")
+    ours = O.gelu_rational(g["z"])
+    assert np.array_equal(ours.view(np.uint32), g["rational"].view(np.uint32))
+
+
+def test_gelu_erf_vs_reference():
+    g = np.load(GOLDEN / "gelu.npz")
+    ours = O.gelu_erf(g["z"]).astype(np.float64)
+    assert np.max(np.abs(ours - g["exact"])) <= 2e-6 * max(1.0, np.max(np.abs(g["exact"])))
+
+
+def test_gelu_rational_approximation_bound():
+    # reference validation/test_ffn.py:91-96
+    z = np.linspace(-10, 10, 10001).astype(np.float32)
+    assert np.max(np.abs(O.gelu_rational(z) - O.gelu_erf(z))) < 2e-5
+
+
+def test_bf16_rounding_ties_and_nan():
+    a = np.array([1.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5, np.nan, np.inf], dtype=np.float32)
+    bits = O.bf16_bits(a)
+    assert bits[0] == 0x3F80 and bits[1] == 0x3F80 and bits[2] == 0x3F82  # ties to even
+    assert np.isnan(O.bf16_to_f32(bits)[4]) and O.bf16_to_f32(bits)[5] == np.inf
+
+
+def _oracle_rows(case_id, rows_override=None):
+    case = C.get_case(case_id)
+    fx = _fixture(case_id)
+    rows = fx["rows"] if rows_override is None else rows_override
+    from tests.golden.make_golden import logical_x_rows
+
+    xr = logical_x_rows(case, rows)
+    w1, w2 = C.weights(case)
+    assert C.digest(xr) == str(fx["x_digest"])
+    assert C.digest(w1) == str(fx["w1_digest"]) and C.digest(w2) == str(fx["w2_digest"])
+    dt = str(fx["dtype"])
+    x, a, b = O.from_bits(xr, dt), O.from_bits(w1, dt), O.from_bits(w2, dt)
+    return fx, dt, x, a, b
+
+
+def assert_pinned(ours_bits, gold_bits, dt, identical=0.98, floor=1e-5):
+    """Oracle and reference agree up to fp32 summation order: at most one unit of the output
+    dtype's relative precision, plus an absolute floor of ``floor`` * max|golden| for outputs
+    that are sums cancelling to near zero; and almost all outputs are bit-identical.  The
+    staged path gets a larger floor: a hidden value whose fp32 sum lands on the other side
+    of a rounding boundary moves by one ulp of the hidden dtype before the down GEMM."""
+    o, g = O.from_bits(ours_bits, dt), O.from_bits(gold_bits, dt)
+    rel = 2.0 ** -7 if dt == "bfloat16" else 2.0 ** -10
+    bound = rel * np.abs(g) + floor * np.abs(g).max()
+    assert np.all(np.abs(o - g) <= bound), float(np.max(np.abs(o - g) - bound))
+    assert (ours_bits == gold_bits).mean() > identical
+
+
+@pytest.mark.parametrize("case_id", FAST)
+def test_oracle_matches_reference_golden(case_id):
+    fx, dt, x, a, b = _oracle_rows(case_id)
+    assert_pinned(O.ffn(x, a, b, dt), fx["golden"], dt)
+    assert_pinned(O.ffn(x, a, b, dt, staged=True, rational=True), fx["staged_rational"], dt, 0.97, 1e-4)
+
+
+@pytest.mark.parametrize("case_id", ["cfg4_bf16", "cfg5_bf16"])
+def test_oracle_matches_reference_golden_large(case_id):
+    fx, dt, x, a, b = _oracle_rows(case_id)
+    assert_pinned(O.ffn(x, a, b, dt), fx["golden"], dt)
+
+
+def test_seeded_inputs_are_deterministic():
+    case = C.get_case("tails_bf16")
+    a = C.make_inputs(case)
+    b = C.make_inputs(case)
+    for s, t in zip(a, b):
+        assert s.shape == t.shape and bool((s == t).all())
+    # X row blocks are independent streams: a sub-range equals the slice of the full draw
+    case = C.get_case("cfg1_fp16")
+    full = C.x_rows(case, 0, 512)
+    assert np.array_equal(C.x_rows(case, 100, 300), full[100:300])
