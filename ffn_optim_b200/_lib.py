@@ -21,6 +21,8 @@ ERR_DEVICE = 4
 ERR_CUDA = 5
 ERR_ALIGNMENT = 6
 ERR_TOO_LARGE = 7
+ERR_SCRATCH = 8
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 DTYPES = {"float16": 0, "bfloat16": 1}
 DOWN_IMPL_CODES = {"basic": 0, "full_load_a": 1, "full_load_b": 2, "streamk": 3}
@@ -32,7 +34,7 @@ KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-b
 EXPORTED = ("ffn_b200_abi_version", "ffn_b200_strerror", "ffn_b200_device_info", "ffn_b200_make_plan",
             "ffn_b200_prepare", "ffn_b200_run", "ffn_b200_rebind_io", "ffn_b200_reset",
             "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_get_plan",
-            "ffn_b200_destroy", "ffn_b200_launch")
+            "ffn_b200_destroy", "ffn_b200_launch", "ffn_b200_run_noalloc")
 
 
 class Problem(ctypes.Structure):
@@ -112,12 +114,12 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             "ffn_b200_get_plan": ([vp, ctypes.POINTER(PlanInfo)], i32),
             "ffn_b200_destroy": ([vp], i32),
             "ffn_b200_launch": ([ctypes.POINTER(Problem), ctypes.POINTER(Buffers), vp], i32),
+            "ffn_b200_run_noalloc": ([ctypes.POINTER(Problem), vp, i64, vp, i64, vp, i64, vp, i64, vp, vp], i32),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
-        del i64
         _lib = lib
         return lib
 

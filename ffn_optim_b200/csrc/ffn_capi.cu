@@ -163,6 +163,8 @@ const char* ffn_b200_strerror(int code) {
     case FFN_B200_ERR_CUDA: return "CUDA call failed";
     case FFN_B200_ERR_ALIGNMENT: return "buffer base not 16-byte aligned or pitch not a multiple of 8 elements";
     case FFN_B200_ERR_TOO_LARGE: return "problem does not fit one launch";
+    case FFN_B200_ERR_SCRATCH:
+      return "problem needs more scratch than the 32 MiB that ffn_b200_run_noalloc holds; use ffn_b200_prepare";
   }
   return "unknown error";
 }
@@ -453,3 +455,16 @@ int ffn_b200_launch(const ffn_b200_problem* pr, const ffn_b200_buffers* b, void*
 }
 
 }  // extern "C"
+
+// Internal accessors used by the allocation-free entry point in ffn_noalloc.cu; not exported.
+namespace ffnb200 {
+void (*internal_kernel_for(int variant, int bf16, int gelu))(const Params) {
+  return kernel_for(variant, bf16, gelu);
+}
+int internal_encode_2d(CUtensorMap* tm, const void* base, int dtype, int64_t inner, int64_t outer, int64_t pitch,
+                       uint32_t box_inner, uint32_t box_outer) {
+  const int rc = get_encode();
+  if (rc) return rc;
+  return encode_2d(tm, base, dtype, inner, outer, pitch, box_inner, box_outer);
+}
+}  // namespace ffnb200

@@ -46,7 +46,8 @@ typedef enum {
   FFN_B200_ERR_DEVICE = 4,         /* not an sm_100 device or block_num > SM count */
   FFN_B200_ERR_CUDA = 5,           /* a CUDA runtime / driver call failed */
   FFN_B200_ERR_ALIGNMENT = 6,      /* base not 16-byte aligned or pitch not a multiple of 8 elements */
-  FFN_B200_ERR_TOO_LARGE = 7       /* tile count does not fit one launch */
+  FFN_B200_ERR_TOO_LARGE = 7,      /* tile count does not fit one launch */
+  FFN_B200_ERR_SCRATCH = 8         /* needs more scratch than ffn_b200_run_noalloc holds */
 } ffn_b200_status;
 
 typedef enum { FFN_B200_F16 = 0, FFN_B200_BF16 = 1 } ffn_b200_dtype;
@@ -160,6 +161,28 @@ FFN_B200_EXPORT int ffn_b200_set_fault_injection(ffn_b200_handle* handle, int mo
 
 FFN_B200_EXPORT int ffn_b200_get_plan(const ffn_b200_handle* handle, ffn_b200_plan* plan);
 FFN_B200_EXPORT int ffn_b200_destroy(ffn_b200_handle* handle);
+
+/* Device scratch held by the library itself for ffn_b200_run_noalloc (hidden activations,
+ * Stream-K partials and synchronisation words of one call). */
+#define FFN_B200_NOALLOC_SCRATCH_BYTES (32ll << 20)
+
+/* Allocation-free run.  No counterpart in the reference: it exists for callers that must
+ * not allocate device memory while they run the FFN -- for example an inference engine that
+ * hands its plugins a fixed memory budget and calls them from its execution path, where a
+ * cudaMalloc would be refused or would synchronise the whole device, or a serving loop that
+ * reserves all memory up front.  The caller passes X, W1, W2 and Y (same layout rules as
+ * ffn_b200_buffers); the hidden tensor, Stream-K partials and counters live in a 32 MiB
+ * array inside the library (FFN_B200_NOALLOC_SCRATCH_BYTES, held by every GPU that loads
+ * this code until the process exits).  Problems whose scratch does not fit return
+ * FFN_B200_ERR_SCRATCH.  `status` is an optional device int32[4] that receives the kernel's
+ * error words (NULL keeps them inside the scratch).  The first call on a device looks up
+ * the array's device address (once per device, with that device current); make that first
+ * call before any stream capture.  Every call clears the counters it needs on `stream` and
+ * then launches once; all calls share the one array, so calls that overlap on the GPU (two
+ * streams, two host threads) race and must be serialised by the caller. */
+FFN_B200_EXPORT int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void* x, int64_t ldx,
+                                         const void* w1, int64_t ldw1, const void* w2, int64_t ldw2, void* y,
+                                         int64_t ldy, int32_t* status, void* stream);
 
 /* One-shot: prepare, clear the scratch words, run once, release the handle. */
 FFN_B200_EXPORT int ffn_b200_launch(const ffn_b200_problem* problem, const ffn_b200_buffers* buffers,
