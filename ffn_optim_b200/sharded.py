@@ -11,9 +11,9 @@ multi-GPU variants of the hot path):
 * **M-sharded** (:class:`RowShardedFFN`): rank r holds rows ``[r*M/P, (r+1)*M/P)`` of X and
   full weights; no communication.
 
-The slicing arithmetic (:func:`h_slice`, :func:`m_slices`, :func:`chunk_rows`) and the
-collective composition (:func:`combine_partials`) are plain functions so they can be
-tested with CPU ``gloo`` ranks.
+The slicing arithmetic (:func:`h_slice`, :func:`m_slices`, :func:`chunk_rows`,
+:func:`scattered_rows`) and the collective composition (:func:`combine_partials`) are
+plain functions so they can be tested with CPU ``gloo`` ranks.
 """
 from __future__ import annotations
 
@@ -21,8 +21,9 @@ from dataclasses import dataclass
 
 
 def h_slice(h: int, rank: int, world: int):
-    """Hidden columns [lo, hi) owned by ``rank``: contiguous, sizes differ by at most 8 and
-    every boundary (but the last) is a multiple of 8 so slices stay 16-byte addressable."""
+    """Hidden columns [lo, hi) owned by ``rank``: contiguous slices of whole 8-column units
+    (so every boundary but H itself is a multiple of 8 and slices stay 16-byte addressable);
+    sizes differ by at most one unit plus the ragged end of H (< 16 columns)."""
     units = (h + 7) // 8
     base, extra = divmod(units, world)
     lo_u = rank * base + min(rank, extra)
@@ -55,6 +56,16 @@ def chunk_rows(m: int, world: int, chunks: int):
         out.append((lo, hi))
         lo = hi
     return out
+
+
+def scattered_rows(chunks, rank: int, world: int):
+    """Global row indices a rank holds after the per-chunk reduce-scatters, in order."""
+    idx = []
+    for lo, hi in chunks:
+        per = (hi - lo) // world
+        start = lo + rank * per
+        idx.extend(range(start, start + per))
+    return idx
 
 
 def combine_partials(partial, out, mode="reduce_scatter", group=None, async_op=False):
@@ -142,12 +153,7 @@ class TensorParallelFFN:
 
     def local_rows(self):
         """Global row indices of the reduce-scatter output on this rank, in output order."""
-        idx = []
-        for ch in self.chunks:
-            per = (ch.hi - ch.lo) // self.world
-            start = ch.lo + self.rank * per
-            idx.extend(range(start, start + per))
-        return idx
+        return scattered_rows([(c.lo, c.hi) for c in self.chunks], self.rank, self.world)
 
     def check(self):
         for ch in self.chunks:
