@@ -37,12 +37,13 @@ METRIC = "fused FFN useful TFLOP/s and µs/call at 1/2/4/8 B200; % of bf16 TC pe
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="cfg5_bf16")
     ap.add_argument("--shard", choices=("h", "m"), default="h")
     ap.add_argument("--chunks", type=int, default=4)
+    ap.add_argument("--tile", default=None, help="force a kernel variant (see ffn_optim_b200._lib.TILE_VARIANTS)")
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -165,6 +166,12 @@ def cpu_oracle_sample(p, x_rows_bits, w1_bits, w2_bits, repeats=1):
     return fl / best / 1e12, best
 
 
+def _lib_variants():
+    from ffn_optim_b200 import _lib
+
+    return _lib.TILE_VARIANTS
+
+
 def to_bits(t):
     import numpy as np
     import torch
@@ -236,7 +243,7 @@ def main():
     down = case.get("down_impl", "basic")
 
     if world == 1:
-        runner = prepare_ffn(x, w1, w2, down_impl=down)
+        runner = prepare_ffn(x, w1, w2, down_impl=down, tile=args.tile)
         launches = 1
         kernel_runs = lambda: runner.run()  # noqa: E731
         check = runner.check
@@ -244,7 +251,7 @@ def main():
     elif args.shard == "h":
         from ffn_optim_b200.sharded import TensorParallelFFN
 
-        runner = TensorParallelFFN(x, w1, w2, chunks=args.chunks, down_impl=down)
+        runner = TensorParallelFFN(x, w1, w2, chunks=args.chunks, down_impl=down, tile=args.tile)
         launches = runner.launches_per_run()
         kernel_runs = runner.run
         check = runner.check
@@ -252,7 +259,7 @@ def main():
     else:
         from ffn_optim_b200.sharded import RowShardedFFN
 
-        runner = RowShardedFFN(x, w1, w2, down_impl=down)
+        runner = RowShardedFFN(x, w1, w2, down_impl=down, tile=args.tile)
         launches = 1
         kernel_runs = runner.run
         check = runner.check
@@ -319,6 +326,9 @@ def main():
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
                "sample": f"{rows} of {p.m} rows of {args.workload} (full weights), {sec:.1f} s, numpy float32 BLAS"}
 
+    first = runner if world == 1 else (runner.chunks[0].prepared if parallelism.startswith("tp") else runner.prepared)
+    block_num = first.plan.block_num
+    variant = {v: k for k, v in _lib_variants().items()}.get(first.plan.kernel["variant"] + 1)
     burst, sustained, hbm, src = peaks()
     per_launch_ms = ms_step / launches
     flops_launch = fl / world / launches if parallelism.startswith("tp") else fl / world
@@ -334,7 +344,7 @@ def main():
                 "vs_baseline": None, "dtype": "bf16" if p.dtype == "bfloat16" else "f16", "data": "synthetic",
                 "config": {"workload": args.workload, "x": list(p.input_shape), "w1": [p.h, p.k], "w2": [p.n, p.h],
                            "down_impl": down, "parallelism": parallelism,
-                           "block_num": getattr(getattr(runner, "plan", None), "block_num", None),
+                           "block_num": block_num, "kernel_variant": variant,
                            "l2": "inputs larger than L2, no flush"},
                 "gpu_launches": launches * args.steps, "clocks": clocks, "roofline": roofline,
                 "e2e": e2e, "cpu_baseline": cpu}

@@ -27,6 +27,8 @@ NOALLOC_SCRATCH_BYTES = 32 << 20
 DTYPES = {"float16": 0, "bfloat16": 1}
 DOWN_IMPL_CODES = {"basic": 0, "full_load_a": 1, "full_load_b": 2, "streamk": 3}
 GELU_CODES = {"rational": 0, "erf": 1}
+# Kernel variants selectable through prepare_ffn(..., tile=...) (None = automatic).
+TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",
                  3: "Stream-K partial wait timed out"}
 
@@ -40,7 +42,7 @@ EXPORTED = ("ffn_b200_abi_version", "ffn_b200_strerror", "ffn_b200_device_info",
 class Problem(ctypes.Structure):
     _fields_ = [("m", ctypes.c_int64), ("k", ctypes.c_int64), ("h", ctypes.c_int64), ("n", ctypes.c_int64),
                 ("dtype", ctypes.c_int32), ("down_impl", ctypes.c_int32), ("gelu", ctypes.c_int32),
-                ("block_num", ctypes.c_int32), ("sm_count", ctypes.c_int32)]
+                ("block_num", ctypes.c_int32), ("sm_count", ctypes.c_int32), ("tile_variant", ctypes.c_int32)]
 
 
 class PhasePlan(ctypes.Structure):
@@ -52,7 +54,8 @@ class PhasePlan(ctypes.Structure):
 
 
 class PlanInfo(ctypes.Structure):
-    _fields_ = [("variant", ctypes.c_int32), ("swap_ab", ctypes.c_int32), ("tile_m", ctypes.c_int32),
+    _fields_ = [("variant", ctypes.c_int32), ("swap_ab", ctypes.c_int32), ("cta_pair", ctypes.c_int32),
+                ("tile_m", ctypes.c_int32),
                 ("tile_n", ctypes.c_int32), ("tile_k", ctypes.c_int32), ("stages", ctypes.c_int32),
                 ("block_num", ctypes.c_int32), ("tmem_cols", ctypes.c_int32), ("smem_bytes", ctypes.c_int64),
                 ("up", PhasePlan), ("down", PhasePlan), ("workspace_floats", ctypes.c_int64),

@@ -121,13 +121,14 @@ def _map_prepare_error(rc):
 
 
 def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", block_num=None,
-                layout="linear", gelu="rational"):
+                layout="linear", gelu="rational", tile=None):
     """Validates, plans and prepares storage and the launch handle without launching the FFN
     (reference ops/api.py:48-89).
 
     ``block_num`` is the persistent CTA count, at most the device's SM count (default: all
     SMs).  ``gelu`` selects the epilogue GELU: 'rational' (the reference kernel's clipped
-    rational erf) or 'erf' (CUDA ``erff``).  Storage copies are device work timed
+    rational erf) or 'erf' (CUDA ``erff``).  ``tile`` forces a kernel variant (see
+    ``make_plan``); None chooses automatically.  Storage copies are device work timed
     separately as ``preparation['auxiliary_device_interval_ms']``.
     """
     import torch
@@ -139,7 +140,7 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
     except (OSError, RuntimeError) as exc:
         raise KernelCompilationError(f"{type(exc).__name__}: {exc}") from exc
     props = torch.cuda.get_device_properties(x.device)
-    plan = make_plan(p, selection, block_num, gelu=gelu, sm_count=props.multi_processor_count)
+    plan = make_plan(p, selection, block_num, gelu=gelu, sm_count=props.multi_processor_count, tile=tile)
     if (props.major, props.minor) != (10, 0):
         raise RuntimeError("This implementation targets B200 (sm_100) only")
     if plan.block_num > props.multi_processor_count:
@@ -157,7 +158,8 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
                             hidden.data_ptr(), hidden.stride(0), out.data_ptr(), out.stride(0), ws.data_ptr(),
                             counters.data_ptr(), flags.data_ptr(), status.data_ptr())
         prob = _lib.Problem(p.m, p.k, p.h, p.n, _lib.DTYPES[p.dtype], _lib.DOWN_IMPL_CODES[down_impl],
-                            _lib.GELU_CODES[gelu], plan.block_num, props.multi_processor_count)
+                            _lib.GELU_CODES[gelu], plan.block_num, props.multi_processor_count,
+                            _lib.TILE_VARIANTS[tile] if tile else 0)
         handle = ctypes.c_void_p()
         before = perf_counter()
         rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), x.device.index or 0, ctypes.byref(handle))

@@ -27,33 +27,37 @@ using KernelFn = void (*)(const Params);
 
 struct Variant {
   int bn, stages;
-  bool swap;
+  bool swap, pair;
 };
-// 0: prefill tiles 128x256, 1: 128x128 for small grids, 2/3: swap-AB decode tiles.
-constexpr Variant kVariants[] = {{256, 4, false}, {128, 6, false}, {16, 8, true}, {64, 8, true}};
-constexpr int kNumVariants = 4;
+// 0: prefill tiles 128x256 (one CTA), 1: 128x128 for small grids, 2/3: swap-AB decode
+// tiles (16 / 64 tokens), 4: prefill tiles 256x256 computed by a CTA pair (cta_group::2).
+constexpr Variant kVariants[] = {{256, 4, false, false}, {128, 6, false, false}, {16, 8, true, false},
+                                 {64, 8, true, false}, {256, 6, false, true}};
+constexpr int kNumVariants = 5;
 
-template <int BN, int ST, bool SW>
+template <int BN, int ST, bool SW, bool PR>
 KernelFn pick_kernel(int bf16, int gelu) {
   using namespace ffnb200;
-  if (bf16) return gelu ? ffn_fused_kernel<BN, ST, SW, true, 1> : ffn_fused_kernel<BN, ST, SW, true, 0>;
-  return gelu ? ffn_fused_kernel<BN, ST, SW, false, 1> : ffn_fused_kernel<BN, ST, SW, false, 0>;
+  if (bf16) return gelu ? ffn_fused_kernel<BN, ST, SW, PR, true, 1> : ffn_fused_kernel<BN, ST, SW, PR, true, 0>;
+  return gelu ? ffn_fused_kernel<BN, ST, SW, PR, false, 1> : ffn_fused_kernel<BN, ST, SW, PR, false, 0>;
 }
 KernelFn kernel_for(int variant, int bf16, int gelu) {
   switch (variant) {
-    case 0: return pick_kernel<256, 4, false>(bf16, gelu);
-    case 1: return pick_kernel<128, 6, false>(bf16, gelu);
-    case 2: return pick_kernel<16, 8, true>(bf16, gelu);
-    case 3: return pick_kernel<64, 8, true>(bf16, gelu);
+    case 0: return pick_kernel<256, 4, false, false>(bf16, gelu);
+    case 1: return pick_kernel<128, 6, false, false>(bf16, gelu);
+    case 2: return pick_kernel<16, 8, true, false>(bf16, gelu);
+    case 3: return pick_kernel<64, 8, true, false>(bf16, gelu);
+    case 4: return pick_kernel<256, 6, false, true>(bf16, gelu);
   }
   return nullptr;
 }
 int smem_for(int variant) {
   switch (variant) {
-    case 0: return ffnb200::Layout<256, 4, false>::kSmem;
-    case 1: return ffnb200::Layout<128, 6, false>::kSmem;
-    case 2: return ffnb200::Layout<16, 8, true>::kSmem;
-    case 3: return ffnb200::Layout<64, 8, true>::kSmem;
+    case 0: return ffnb200::Layout<256, 4, false, false>::kSmem;
+    case 1: return ffnb200::Layout<128, 6, false, false>::kSmem;
+    case 2: return ffnb200::Layout<16, 8, true, false>::kSmem;
+    case 3: return ffnb200::Layout<64, 8, true, false>::kSmem;
+    case 4: return ffnb200::Layout<256, 6, false, true>::kSmem;
   }
   return 0;
 }
@@ -71,8 +75,8 @@ struct PhaseInput {
 // Fills one phase's schedule.  split=true applies the Stream-K tail split of the reference
 // (ops/kernel/ffn.py:642-665): sk = T mod C tail tiles, their sk*L k-blocks spread as
 // q = floor(sk*L / C) per CTA with the first (sk*L mod C) CTAs taking one more.
-int phase_plan(const PhaseInput& in, int bn, int C, bool split, ffn_b200_phase_plan* out) {
-  const int64_t tr = cdiv(in.rows, ffnb200::kBM);
+int phase_plan(const PhaseInput& in, int tile_m, int bn, int C, bool split, ffn_b200_phase_plan* out) {
+  const int64_t tr = cdiv(in.rows, tile_m);
   const int64_t tq = cdiv(in.cols, bn);
   const int64_t T = tr * tq;
   const int64_t L = cdiv(in.depth, ffnb200::kBK);
@@ -196,36 +200,44 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
     const int rc = query_sm_count(&sm);
     if (rc) return rc;
   }
-  const int C = pr->block_num > 0 ? pr->block_num : sm;
-  if (C < 1 || C > 65535 || pr->block_num < 0) return FFN_B200_ERR_INVALID;
+  const int grid = pr->block_num > 0 ? pr->block_num : sm;
+  if (grid < 1 || grid > 65535 || pr->block_num < 0) return FFN_B200_ERR_INVALID;
+  if (pr->tile_variant < 0 || pr->tile_variant > kNumVariants) return FFN_B200_ERR_INVALID;
 
   std::memset(out, 0, sizeof(*out));
   int variant;
-  if (pr->m <= 16) {
+  if (pr->tile_variant > 0) {
+    variant = pr->tile_variant - 1;
+    if (kVariants[variant].swap && pr->m > kVariants[variant].bn) return FFN_B200_ERR_INVALID;
+    if (kVariants[variant].pair && grid < 2) return FFN_B200_ERR_INVALID;
+  } else if (pr->m <= 16) {
     variant = 2;
   } else if (pr->m <= 64) {
     variant = 3;
   } else {
     const int64_t t256 = cdiv(pr->m, 128) * cdiv(pr->h, 256);
-    variant = t256 >= 2 * static_cast<int64_t>(C) ? 0 : 1;
+    variant = t256 >= 2 * static_cast<int64_t>(grid) ? 0 : 1;
   }
   const Variant& v = kVariants[variant];
+  const int ncta = v.pair ? 2 : 1;
+  const int tile_m = ffnb200::kBM * ncta;
+  const int C = grid / ncta;  // work-list owners (CTAs, or CTA pairs)
   const PhaseInput up = v.swap ? PhaseInput{pr->h, pr->m, pr->k} : PhaseInput{pr->m, pr->h, pr->k};
   const PhaseInput dn = v.swap ? PhaseInput{pr->n, pr->m, pr->h} : PhaseInput{pr->m, pr->n, pr->h};
 
   // Up phase: data-parallel, with the tail wave split along K when whole tiles would leave
   // more than a tenth of the CTAs idle in the last wave (a schedule choice only).
   ffn_b200_phase_plan probe;
-  int rc = phase_plan(up, v.bn, C, false, &probe);
+  int rc = phase_plan(up, tile_m, v.bn, C, false, &probe);
   if (rc) return rc;
   const int64_t waves = cdiv(probe.tiles, C);
   const bool up_split = (probe.tiles % C) != 0 && probe.k_blocks >= 2 &&
                         static_cast<double>(probe.tiles) < 0.9 * static_cast<double>(waves * C);
-  rc = phase_plan(up, v.bn, C, up_split, &out->up);
+  rc = phase_plan(up, tile_m, v.bn, C, up_split, &out->up);
   if (rc) return rc;
 
   const bool streamk = pr->down_impl == FFN_B200_DOWN_STREAMK;
-  rc = phase_plan(dn, v.bn, C, streamk, &out->down);
+  rc = phase_plan(dn, tile_m, v.bn, C, streamk, &out->down);
   if (rc) return rc;
   if (streamk && (out->down.tiles % C == 0 || out->down.k_blocks < 2)) return FFN_B200_ERR_NOT_APPLICABLE;
   if (static_cast<int64_t>(out->up.sk_tiles) * out->up.k_blocks >= (int64_t(1) << 31) ||
@@ -234,16 +246,17 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
 
   out->variant = variant;
   out->swap_ab = v.swap ? 1 : 0;
-  out->tile_m = ffnb200::kBM;
+  out->cta_pair = v.pair ? 1 : 0;
+  out->tile_m = tile_m;
   out->tile_n = v.bn;
   out->tile_k = ffnb200::kBK;
   out->stages = v.stages;
-  out->block_num = C;
+  out->block_num = C * ncta;
   out->tmem_cols = tmem_cols_for(variant);
   out->smem_bytes = smem_for(variant);
-  out->workspace_floats = 2ll * C * ffnb200::kBM * v.bn;
+  out->workspace_floats = 2ll * C * ncta * ffnb200::kBM * v.bn;
   out->counter_words = v.swap ? out->up.tiles_q : out->up.tiles_r;
-  out->flag_words = 2ll * C;
+  out->flag_words = 2ll * C * ncta;
   out->status_words = 4;
   return FFN_B200_OK;
 }
@@ -290,7 +303,8 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
 
   Params& P = h->params;
   std::memset(&P, 0, sizeof(P));
-  const uint32_t bn = static_cast<uint32_t>(plan.tile_n);
+  // B boxes: each CTA of a pair loads half of the tile's B rows.
+  const uint32_t bn = static_cast<uint32_t>(plan.tile_n / (plan.cta_pair ? 2 : 1));
   const int dt = prob.dtype;
   const bool sw = plan.swap_ab != 0;
   // Up:   normal A = X [M,K] (128-row boxes), B = W1 [H,K] (bn-row boxes); swap exchanges them.
@@ -331,11 +345,12 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.M = static_cast<int>(prob.m);
   P.H = static_cast<int>(prob.h);
   P.N = static_cast<int>(prob.n);
-  P.C = plan.block_num;
+  const int ncta = plan.cta_pair ? 2 : 1;
+  P.C = plan.block_num / ncta;
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
-  // Readiness counters gain 4 * (up tiles per row block) per launch, flags 4 per launch.
-  const int64_t per_blk = 4ll * (sw ? plan.up.tiles_r : plan.up.tiles_q);
+  // Readiness counters gain 4 * ncta * (up tiles per row block) per launch, flags 4 per launch.
+  const int64_t per_blk = 4ll * ncta * (sw ? plan.up.tiles_r : plan.up.tiles_q);
   h->epoch_limit = static_cast<unsigned>(((int64_t(1) << 30) / (per_blk > 4 ? per_blk : 4)));
 
   int cur = 0;
@@ -343,11 +358,35 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   if (cur != device) cudaSetDevice(device);
   const cudaError_t e =
       cudaFuncSetAttribute(h->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem_bytes));
+  int rc2 = e == cudaSuccess ? FFN_B200_OK : FFN_B200_ERR_CUDA;
+  if (!rc2 && plan.cta_pair) {
+    // Every CTA pair of the persistent grid must be resident at once (the down phase waits
+    // on up tiles of other pairs): the grid may not exceed the co-resident cluster count.
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.block_num), 1, 1);
+    cfg.blockDim = dim3(ffnb200::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(plan.smem_bytes);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, h->kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      rc2 = FFN_B200_ERR_CUDA;
+    } else if (plan.block_num > 2 * clusters) {
+      rc2 = FFN_B200_ERR_DEVICE;
+    }
+  }
   if (cur != device) cudaSetDevice(cur);
-  if (e != cudaSuccess) {
+  if (rc2) {
     cudaGetLastError();
     delete h;
-    return FFN_B200_ERR_CUDA;
+    return rc2;
   }
   *out = h;
   return FFN_B200_OK;
@@ -384,8 +423,15 @@ int ffn_b200_run(ffn_b200_handle* h, void* stream) {
   cfg.dynamicSmemBytes = static_cast<size_t>(h->plan.smem_bytes);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  if (h->plan.cta_pair) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, h->kernel, h->params);

@@ -67,9 +67,9 @@ struct Params {
   void* hidden;
   void* y;
   long long ldh, ldy;    // pitches in elements
-  float* ws;             // [2][C][kBM][BN] fp32 partials
+  float* ws;             // [2][C][ncta][kBM][BN] fp32 partials (one slot per CTA)
   unsigned* counters;    // readiness per token block
-  unsigned* flags;       // [2][C] partial-ready epochs
+  unsigned* flags;       // [2][C][ncta] partial-ready counts (4 per launch)
   int* status;           // [0] code, [1] CTA, [2] aux
   PhaseSched up, dn;
   int M, H, N;
@@ -184,6 +184,64 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
+// ---- CTA-pair (cluster of 2, tcgen05 cta_group::2) forms --------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on an mbarrier of
+// either CTA of the pair (here: the leader's), no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
+                                                 uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem of both CTAs] (+)= A[256 rows: 128 in each CTA] . B[N rows: N/2 in each CTA]^T.
+__device__ __forceinline__ void umma_f16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+      ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrive once on this CTA's mbarrier when the pair MMAs issued so far complete.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Same, arriving on the mbarrier at this shared-memory offset in both CTAs of the pair
+// (tcgen05.commit signal fan-out; this is not a data load and reads no memory).
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               ::"r"(bar), "h"(static_cast<uint16_t>(0x3))
+               : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns; the wait is in the same asm block so the
 // outputs are never consumed before the load has landed.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
@@ -223,11 +281,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
          (static_cast<uint64_t>(2) << 61);
 }
-// Instruction descriptor for kind::f16: D fp32, A/B fp16 or bf16, both K-major, M=128.
-template <bool BF16, int N>
+// Instruction descriptor for kind::f16: D fp32, A/B fp16 or bf16, both K-major, M x N.
+template <bool BF16, int N, int M>
 __host__ __device__ constexpr uint32_t make_idesc() {
   return (1u << 4) | ((BF16 ? 1u : 0u) << 7) | ((BF16 ? 1u : 0u) << 10) |
-         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -389,9 +447,11 @@ __device__ __forceinline__ bool wait_word_ge(const unsigned* word, unsigned targ
 // ------------------------------------------------------------------------------------------
 // The kernel
 // ------------------------------------------------------------------------------------------
-template <int BN, int STAGES, bool SWAP>
+template <int BN, int STAGES, bool SWAP, bool PAIR = false>
 struct Layout {
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kNcta = PAIR ? 2 : 1;       // CTAs per tile (cluster size)
+  static constexpr int kBRows = BN / kNcta;         // B rows each CTA loads per stage
+  static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBytes = SWAP ? 0 : 4 * 2 * kStageBufBytes;
   static constexpr int kBarBytes = 256;
@@ -399,12 +459,21 @@ struct Layout {
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static_assert((kBBytes % 1024) == 0, "B tile must be whole swizzle atoms");
   static_assert((2 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");
+  static_assert(!PAIR || !SWAP, "CTA pairs are used for prefill tiles only");
 };
 
-template <int BN, int STAGES, bool SWAP, bool BF16, int GELU>
+// PAIR = true: a cluster of two CTAs computes one 256 x BN tile with tcgen05 cta_group::2.
+// Each CTA loads 128 rows of A and BN/2 rows of B into its own shared memory (plain TMA
+// loads, no multicast) and completes the transaction bytes on the leader's (rank 0) full
+// barrier; the leader's MMA thread issues the pair MMAs, whose D lands 128 rows in each
+// CTA's TMEM, and its tcgen05.commit arrives on the empty / tmem-full barriers of both CTAs;
+// each CTA's epilogue stores its own 128 rows and releases the accumulator on the leader.
+template <int BN, int STAGES, bool SWAP, bool PAIR, bool BF16, int GELU>
 __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_constant__ Params p) {
-  using LY = Layout<BN, STAGES, SWAP>;
-  constexpr uint32_t kIdesc = make_idesc<BF16, BN>();
+  using LY = Layout<BN, STAGES, SWAP, PAIR>;
+  constexpr int kNcta = LY::kNcta;
+  constexpr int kTileM = kBM * kNcta;
+  constexpr uint32_t kIdesc = make_idesc<BF16, BN, kTileM>();
   static_assert(SWAP || (BN % 64) == 0, "normal mode stores 64-column chunks");
   static_assert(!SWAP || (BN % 16) == 0, "swap mode loads 16-column chunks");
 
@@ -426,7 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int cta = blockIdx.x;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  const int cta = static_cast<int>(blockIdx.x) / kNcta;  // work-list owner (one per tile-sized group)
+  const int slot_base = static_cast<int>(rank);          // partial / flag slot = (phase*C + cta)*kNcta + rank
 
   if (threadIdx.x == 0) {
 #pragma unroll 1
@@ -436,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), kEpiThreads);
+      mbar_init(tempty_bar(a), kEpiThreads * kNcta);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -448,11 +520,17 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
     prefetch_tmap(&p.tm_a_dn); prefetch_tmap(&p.tm_b_dn);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), LY::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), LY::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), LY::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // peer barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -463,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       uint32_t phase = 0;
       long long issued = 0;
       int ready_blk = -1;
-      const unsigned per_blk = 4u * static_cast<unsigned>(SWAP ? p.up.tiles_r : p.up.tiles_q);
+      const unsigned per_blk = 4u * kNcta * static_cast<unsigned>(SWAP ? p.up.tiles_r : p.up.tiles_q);
       const unsigned target = p.epoch * per_blk + (p.inject ? 1u : 0u);
       bool ok = true;
 #pragma unroll 1
@@ -483,31 +561,43 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
             ready_blk = blk;
           }
         }
+        const int arow = tr * kTileM + static_cast<int>(rank) * kBM;
+        const int brow = tq * BN + static_cast<int>(rank) * LY::kBRows;
 #pragma unroll 1
         for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) { ok = false; break; }
-          mbar_expect_tx(full_bar(stage), LY::kStageBytes);
-          tma_load_2d(sA + stage * kABytes, ta, kb * kBK, tr * kBM, full_bar(stage));
-          tma_load_2d(sB + stage * LY::kBBytes, tb, kb * kBK, tq * BN, full_bar(stage));
+          if constexpr (PAIR) {
+            const uint32_t fb = map_to_rank(full_bar(stage), 0);
+            if (leader) mbar_expect_tx(full_bar(stage), kNcta * LY::kStageBytes);
+            tma_load_2d_pair(sA + stage * kABytes, ta, kb * kBK, arow, fb);
+            tma_load_2d_pair(sB + stage * LY::kBBytes, tb, kb * kBK, brow, fb);
+          } else {
+            mbar_expect_tx(full_bar(stage), LY::kStageBytes);
+            tma_load_2d(sA + stage * kABytes, ta, kb * kBK, arow, full_bar(stage));
+            tma_load_2d(sB + stage * LY::kBBytes, tb, kb * kBK, brow, full_bar(stage));
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
-      // Drain: every issued load must land before the CTA may exit.
-      const long long first = issued > STAGES ? issued - STAGES : 0;
+      // Drain: every issued load must land before the CTA may exit.  In a pair the
+      // transaction bytes land on the leader's barriers, so the leader drains for both.
+      if (leader) {
+        const long long first = issued > STAGES ? issued - STAGES : 0;
 #pragma unroll 1
-      for (long long i = first; i < issued; ++i) {
-        const int s = static_cast<int>(i % STAGES);
-        const uint32_t par = static_cast<uint32_t>((i / STAGES) & 1);
-        const uint64_t t0 = gtimer();
-        while (!mbar_try_wait(full_bar(s), par)) {
-          if (gtimer() - t0 > p.wait_limit_ns) break;
+        for (long long i = first; i < issued; ++i) {
+          const int s = static_cast<int>(i % STAGES);
+          const uint32_t par = static_cast<uint32_t>((i / STAGES) & 1);
+          const uint64_t t0 = gtimer();
+          while (!mbar_try_wait(full_bar(s), par)) {
+            if (gtimer() - t0 > p.wait_limit_ns) break;
+          }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer (leader)
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -529,17 +619,28 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             // +32 bytes along K inside the 128-byte swizzle atom = +2 in the 16-byte address field
-            umma_f16(d, da + 2 * k, db + 2 * k, kIdesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+            const uint32_t accum = (kb > u.kb0 || k > 0) ? 1u : 0u;
+            if constexpr (PAIR) umma_f16_pair(d, da + 2 * k, db + 2 * k, kIdesc, accum);
+            else umma_f16(d, da + 2 * k, db + 2 * k, kIdesc, accum);
           }
-          umma_commit(empty_bar(stage));
+          if constexpr (PAIR) {
+            umma_commit_pair_both(empty_bar(stage));
+          } else {
+            umma_commit(empty_bar(stage));
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        umma_commit(tfull_bar(acc));
+        if constexpr (PAIR) {
+          umma_commit_pair_both(tfull_bar(acc));
+        } else {
+          umma_commit(tfull_bar(acc));
+        }
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
       // Drain: all issued MMAs complete before TMEM is released.
-      umma_commit(drain_bar);
+      if constexpr (PAIR) umma_commit_pair(drain_bar);
+      else umma_commit(drain_bar);
       const uint64_t t0 = gtimer();
       while (!mbar_try_wait(drain_bar, 0)) {
         if (gtimer() - t0 > p.wait_limit_ns) break;
@@ -549,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     const int ew = warp - 2;            // staging-buffer owner index
     const int sub = warp & 3;           // TMEM lane sub-partition this warp may access
-    const int row = sub * 32 + lane;    // row inside the 128-row tile
+    const int row = sub * 32 + lane;    // row inside this CTA's 128 rows of the tile
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
@@ -565,22 +666,28 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      // Stream-K owner: wait for every contributor's partial of this tile.
+      // Stream-K owner: wait for every contributor's partial of this tile (same pair rank).
       if (u.role == kRoleOwner && u.c_first <= u.c_last) {
         if (lane == 0) {
           for (int c2 = u.c_first; c2 <= u.c_last && ok; ++c2)
-            ok = wait_word_ge(p.flags + u.phase * p.C + c2, 4u * p.epoch, abort_flag, p, 3, c2) ? 1 : 0;
+            ok = wait_word_ge(p.flags + (u.phase * p.C + c2) * kNcta + slot_base, 4u * p.epoch, abort_flag, p, 3,
+                              c2) ? 1 : 0;
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
-        for (int c2 = u.c_first; c2 <= u.c_last; ++c2) (void)ld_acquire(p.flags + u.phase * p.C + c2);
+        for (int c2 = u.c_first; c2 <= u.c_last; ++c2)
+          (void)ld_acquire(p.flags + (u.phase * p.C + c2) * kNcta + slot_base);
       }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      float* ws_own = p.ws + (static_cast<size_t>(u.phase * p.C + cta) * kBM + row) * BN;
+      auto ws_row = [&](int c) {
+        return p.ws + (static_cast<size_t>((u.phase * p.C + c) * kNcta + slot_base) * kBM + row) * BN;
+      };
+      float* ws_own = ws_row(cta);
 
       if constexpr (!SWAP) {
         // Normal mode: tile rows are tokens, columns are features (H for up, N for down).
         const CUtensorMap* tms = u.phase ? &p.tm_st_y : &p.tm_st_hid;
+        const int orow = tr * kTileM + static_cast<int>(rank) * kBM + sub * 32;
 #pragma unroll 1
         for (int ch = 0; ch < BN / 64; ++ch) {
           float v[64];
@@ -595,8 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
           if (u.role == kRoleOwner) {
 #pragma unroll 1
             for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
-              const float4* src = reinterpret_cast<const float4*>(
-                  p.ws + (static_cast<size_t>(u.phase * p.C + c2) * kBM + row) * BN + ch * 64);
+              const float4* src = reinterpret_cast<const float4*>(ws_row(c2) + ch * 64);
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const float4 t = __ldcg(src + j);
@@ -625,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
           fence_async_shared();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(tms, sb, tq * BN + ch * 64, tr * kBM + sub * 32);
+            tma_store_2d(tms, sb, tq * BN + ch * 64, orow);
             bulk_commit();
           }
           sbuf ^= 1;
@@ -649,8 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
           if (u.role == kRoleOwner) {
 #pragma unroll 1
             for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
-              const float4* src = reinterpret_cast<const float4*>(
-                  p.ws + (static_cast<size_t>(u.phase * p.C + c2) * kBM + row) * BN + ch * 16);
+              const float4* src = reinterpret_cast<const float4*>(ws_row(c2) + ch * 16);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const float4 t = __ldcg(src + j);
@@ -670,9 +775,10 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
           }
         }
       }
-      // Release the TMEM accumulator to the MMA warp.
+      // Release the TMEM accumulator to the (leader's) MMA warp.
       tc_fence_before();
-      mbar_arrive(tempty_bar(acc));
+      if constexpr (PAIR) mbar_arrive_cluster(map_to_rank(tempty_bar(acc), 0));
+      else mbar_arrive(tempty_bar(acc));
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
 
       if (u.role == kRoleContrib) {
@@ -680,7 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
         // waits for 4 signals per launch and no CTA-wide barrier is involved.
         __threadfence();
         __syncwarp();
-        if (lane == 0) red_release_add(p.flags + u.phase * p.C + cta, 1u);
+        if (lane == 0) red_release_add(p.flags + (u.phase * p.C + cta) * kNcta + slot_base, 1u);
       } else if (u.phase == 0) {
         // Hidden tile stored: signal the row block (one signal per warp).
         const int blk = SWAP ? tq : tr;
@@ -706,8 +812,12 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal it
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, LY::kTmemCols);
+  if (warp == 1) {
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, LY::kTmemCols);
+    else tmem_dealloc(tmem_base, LY::kTmemCols);
+  }
 }
 
 }  // namespace ffnb200

@@ -89,9 +89,15 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   ffn_b200_problem prob = *problem;
   prob.sm_count = sm;
   if (prob.block_num > sm) return FFN_B200_ERR_DEVICE;
+  if (prob.tile_variant == 5) return FFN_B200_ERR_INVALID;  // CTA-pair tiles need a cluster launch
   ffn_b200_plan plan;
   rc = ffn_b200_make_plan(&prob, &plan);
   if (rc) return rc;
+  if (plan.cta_pair) {  // automatic choice of CTA-pair tiles: use the one-CTA 128x256 tiles here
+    prob.tile_variant = 1;
+    rc = ffn_b200_make_plan(&prob, &plan);
+    if (rc) return rc;
+  }
 
   // Scratch layout: hidden [M, ldh] | fp32 partials | counters | flags | status, 256-B aligned.
   const int64_t ldh = round_up(prob.h, 8);

@@ -90,12 +90,14 @@ def device_sm_count(device=None):
     return B200_SM_COUNT
 
 
-def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational", sm_count=None):
+def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational", sm_count=None, tile=None):
     """Plans one fused launch (reference ops/host/tiling.py:58-74).
 
-    ``block_num`` None means one CTA per SM.  Raises DependencyUnavailable for the
-    full-load variants, NotApplicable for Stream-K without a tail wave (the reference's
-    rule, applied to this kernel's tile grid), ValueError otherwise.
+    ``block_num`` None means one CTA per SM.  ``tile`` None picks the kernel variant
+    automatically; a name of ``_lib.TILE_VARIANTS`` forces one (tests, benchmarks).  Raises
+    DependencyUnavailable for the full-load variants, NotApplicable for Stream-K without a
+    tail wave (the reference's rule, applied to this kernel's tile grid), ValueError
+    otherwise.
     """
     from .. import _lib
 
@@ -107,9 +109,12 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
         raise ValueError("block_num must be a positive integer; hardware limit checked before launch")
     if gelu not in _lib.GELU_CODES:
         raise ValueError(f"gelu must be one of {sorted(_lib.GELU_CODES)}")
+    if tile is not None and tile not in _lib.TILE_VARIANTS:
+        raise ValueError(f"tile must be None or one of {sorted(_lib.TILE_VARIANTS)}")
     lib = _lib.load()
     prob = _lib.Problem(problem.m, problem.k, problem.h, problem.n, _lib.DTYPES[problem.dtype],
-                        _lib.DOWN_IMPL_CODES[selection.down_impl], _lib.GELU_CODES[gelu], block_num, sms)
+                        _lib.DOWN_IMPL_CODES[selection.down_impl], _lib.GELU_CODES[gelu], block_num, sms,
+                        _lib.TILE_VARIANTS[tile] if tile else 0)
     info = _lib.PlanInfo()
     rc = lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info))
     if rc == _lib.ERR_NOT_APPLICABLE:
@@ -122,5 +127,5 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
     kernel = info.to_dict()
     up = Tile(info.tile_m, info.tile_n, info.tile_k, info.stages)
     down = Tile(info.tile_m, info.tile_n, info.tile_k, info.stages)
-    ws_shape = (2 * block_num * info.tile_m, info.tile_n)
-    return Plan(problem, selection, block_num, up, down, ws_shape, gelu, kernel)
+    ws_shape = (2 * info.block_num * 128, info.tile_n)
+    return Plan(problem, selection, info.block_num, up, down, ws_shape, gelu, kernel)

@@ -98,7 +98,7 @@ class TensorParallelFFN:
     """
 
     def __init__(self, x, w1, w2, *, group=None, mode="reduce_scatter", chunks=4, sliced=False,
-                 down_impl="basic", block_num=None, gelu="rational"):
+                 down_impl="basic", block_num=None, gelu="rational", tile=None):
         import torch
         import torch.distributed as dist
 
@@ -125,7 +125,7 @@ class TensorParallelFFN:
         rows = chunk_rows(m, self.world, chunks) if mode == "reduce_scatter" else [(0, m)]
         self.chunks = []
         for lo, hi in rows:
-            prepared = prepare_ffn(x2[lo:hi], w1, w2, down_impl=down_impl, block_num=block_num, gelu=gelu)
+            prepared = prepare_ffn(x2[lo:hi], w1, w2, down_impl=down_impl, block_num=block_num, gelu=gelu, tile=tile)
             out = None
             if mode == "reduce_scatter":
                 out = torch.empty(((hi - lo) // self.world, self.n), dtype=x.dtype, device=x.device)
@@ -165,7 +165,7 @@ class RowShardedFFN:
     no communication.  :meth:`run` returns this rank's rows of Y."""
 
     def __init__(self, x, w1, w2, *, group=None, down_impl="basic", block_num=None, gelu="rational",
-                 local=False):
+                 local=False, tile=None):
         import torch.distributed as dist
 
         from .api import prepare_ffn
@@ -180,7 +180,7 @@ class RowShardedFFN:
         else:
             self.lo, self.hi = m_slices(m, self.world)[self.rank]
             x_local = x.reshape(m, k)[self.lo:self.hi]
-        self.prepared = prepare_ffn(x_local, w1, w2, down_impl=down_impl, block_num=block_num, gelu=gelu)
+        self.prepared = prepare_ffn(x_local, w1, w2, down_impl=down_impl, block_num=block_num, gelu=gelu, tile=tile)
 
     def launches_per_run(self):
         return 1

@@ -80,6 +80,8 @@ typedef struct {
   int32_t gelu;        /* ffn_b200_gelu */
   int32_t block_num;   /* persistent CTA count; 0 = one per SM */
   int32_t sm_count;    /* SMs of the target device; 0 = query the current device */
+  int32_t tile_variant; /* 0 = automatic; 1 + variant id forces one kernel variant
+                           (1: 128x256, 2: 128x128, 3: swap 16, 4: swap 64, 5: CTA pair 256x256) */
 } ffn_b200_problem;
 
 /* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
@@ -96,8 +98,9 @@ typedef struct {
 typedef struct {
   int32_t variant;       /* kernel instantiation id */
   int32_t swap_ab;       /* 1: weights are the MMA's M operand and tokens its N (small M) */
+  int32_t cta_pair;      /* 1: a cluster of two CTAs computes each tile (tcgen05 cta_group::2) */
   int32_t tile_m, tile_n, tile_k, stages;
-  int32_t block_num;
+  int32_t block_num;     /* CTAs launched (even for CTA pairs) */
   int32_t tmem_cols;
   int64_t smem_bytes;
   ffn_b200_phase_plan up, down;

@@ -117,13 +117,14 @@ def _large_inputs(case, fixture_rows):
     return x.view(p.input_shape), w1, w2, w1b, w2b
 
 
+@pytest.mark.parametrize("tile", [None, "pair256x256", "cta128x256"])
 @pytest.mark.parametrize("case_id", ["cfg4_bf16", "cfg5_bf16"])
-def test_full_size_vs_golden_and_oracle(case_id):
+def test_full_size_vs_golden_and_oracle(case_id, tile):
     case = C.get_case(case_id)
     fx = np.load(GOLDEN / f"{case_id}.npz")
     p = C.case_problem(case)
     x, w1, w2, w1b, w2b = _large_inputs(case, fx["rows"])
-    prepared, y = run(x, w1, w2, down_impl=case["down_impl"])
+    prepared, y = run(x, w1, w2, down_impl=case["down_impl"], tile=tile)
     got = rows_of(y, fx["rows"])
     assert_close_bits(got, fx["staged_rational"], p.dtype)
     assert_criterion(got, fx["golden"], p.dtype)
@@ -156,14 +157,15 @@ RAGGED = [
 
 @pytest.mark.parametrize("shape", RAGGED, ids=lambda s: "x".join(map(str, s[:4])) + str(s[4])[-4:])
 @pytest.mark.parametrize("down_impl", ["basic", "streamk"])
-def test_ragged_shapes_vs_oracle(shape, down_impl):
+@pytest.mark.parametrize("tile", [None, "pair256x256", "cta128x128"])
+def test_ragged_shapes_vs_oracle(shape, down_impl, tile):
     m, k, h, n, dtype = shape
     g = torch.Generator().manual_seed(m * 31 + k)
     x = torch.randn(m, k, generator=g).to(dtype)
     w1 = (torch.randn(h, k, generator=g) * k ** -0.5).to(dtype)
     w2 = (torch.randn(n, h, generator=g) * h ** -0.5).to(dtype)
     try:
-        _, y = run(x.cuda(), w1.cuda(), w2.cuda(), down_impl=down_impl)
+        _, y = run(x.cuda(), w1.cuda(), w2.cuda(), down_impl=down_impl, tile=tile)
     except NotApplicable:
         pytest.skip("Stream-K not applicable")
     dt = str(dtype).removeprefix("torch.")

@@ -127,17 +127,23 @@ def _units(phase, C):
 
 
 @pytest.mark.parametrize("case_id", [c["case_id"] for c in C.load_cases()])
-def test_plan_covers_every_k_block_once(case_id):
+@pytest.mark.parametrize("tile", [None, "pair256x256"])
+def test_plan_covers_every_k_block_once(case_id, tile):
     case = C.get_case(case_id)
     p = C.case_problem(case)
+    if tile and p.m <= 64:
+        pytest.skip("CTA-pair tiles are prefill tiles")
     for down in ("basic", "streamk"):
         try:
-            plan = make_plan(p, Selection(down_impl=down), sm_count=148)
+            plan = make_plan(p, Selection(down_impl=down), sm_count=148, tile=tile)
         except NotApplicable:
             assert down == "streamk"
             continue
         k = plan.kernel
         assert k["block_num"] == 148
+        owners_n = 148 // (2 if k["cta_pair"] else 1)
+        if tile:
+            assert k["cta_pair"] == 1 and k["tile_m"] == 256 and k["up"]["tiles_r"] == -(-p.m // 256)
         if p.m <= 16:
             assert k["swap_ab"] == 1 and k["tile_n"] == 16
         elif p.m <= 64:
@@ -147,7 +153,7 @@ def test_plan_covers_every_k_block_once(case_id):
             assert ph["tiles"] == ph["tiles_r"] * ph["tiles_q"]
             cover = {}
             owners = {}
-            for c, t, a, b, role in _units(ph, 148):
+            for c, t, a, b, role in _units(ph, owners_n):
                 for kb in range(a, b):
                     cover[(t, kb)] = cover.get((t, kb), 0) + 1
                 if role in ("full", "owner"):
