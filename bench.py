@@ -32,6 +32,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "fused FFN useful TFLOP/s and µs/call at 1/2/4/8 B200; % of bf16 TC peak"
+L2_BYTES = 128 << 20
 
 
 def parse():
@@ -45,6 +46,8 @@ def parse():
     ap.add_argument("--chunks", type=int, default=4)
     ap.add_argument("--tile", default=None, help="force a kernel variant (see ffn_optim_b200._lib.TILE_VARIANTS)")
     ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--flush", choices=("auto", "on", "off"), default="auto",
+                    help="flush L2 between timed steps (auto: when the operands fit in 2x L2)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
@@ -273,19 +276,36 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    unique_bytes = 2 * (p.m * p.k + p.h * p.k + p.n * p.h + p.m * p.n)
+    flush = args.flush == "on" or (args.flush == "auto" and unique_bytes < 2 * L2_BYTES)
+    scrub = torch.empty(4 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
     sampler = ClockSampler(local)
     sampler.start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.steps):
-        kernel_runs()
-    end.record()
-    end.synchronize()
+    if flush:
+        # Each step timed alone; an L2-sized write between steps evicts the operands.
+        ms = 0.0
+        pairs = []
+        for _ in range(args.steps):
+            scrub.fill_(1.0)
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            kernel_runs()
+            e0.record()
+            pairs.append((s0, e0))
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in pairs)
+    else:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            kernel_runs()
+        end.record()
+        end.synchronize()
+        ms = start.elapsed_time(end)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop()
-    ms = start.elapsed_time(end)
     check()
     t = torch.tensor([ms], device=dev)
     if world > 1:
@@ -345,7 +365,7 @@ def main():
                 "config": {"workload": args.workload, "x": list(p.input_shape), "w1": [p.h, p.k], "w2": [p.n, p.h],
                            "down_impl": down, "parallelism": parallelism,
                            "block_num": block_num, "kernel_variant": variant,
-                           "l2": "inputs larger than L2, no flush"},
+                           "l2": "L2 flushed between steps (512 MB write)" if flush else "inputs larger than L2, no flush"},
                 "gpu_launches": launches * args.steps, "clocks": clocks, "roofline": roofline,
                 "e2e": e2e, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)

@@ -29,20 +29,22 @@ DOWN_IMPL_CODES = {"basic": 0, "full_load_a": 1, "full_load_b": 2, "streamk": 3}
 GELU_CODES = {"rational": 0, "erf": 1}
 # Kernel variants selectable through prepare_ffn(..., tile=...) (None = automatic).
 TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5}
+L2_POLICIES = {"none": 1, "stream_b": 2}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",
                  3: "Stream-K partial wait timed out"}
 
 # Every symbol the header declares; the CPU tests check the library exports all of them.
 EXPORTED = ("ffn_b200_abi_version", "ffn_b200_strerror", "ffn_b200_device_info", "ffn_b200_make_plan",
             "ffn_b200_prepare", "ffn_b200_run", "ffn_b200_rebind_io", "ffn_b200_reset",
-            "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_get_plan",
+            "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_set_trace", "ffn_b200_get_plan",
             "ffn_b200_destroy", "ffn_b200_launch", "ffn_b200_run_noalloc")
 
 
 class Problem(ctypes.Structure):
     _fields_ = [("m", ctypes.c_int64), ("k", ctypes.c_int64), ("h", ctypes.c_int64), ("n", ctypes.c_int64),
                 ("dtype", ctypes.c_int32), ("down_impl", ctypes.c_int32), ("gelu", ctypes.c_int32),
-                ("block_num", ctypes.c_int32), ("sm_count", ctypes.c_int32), ("tile_variant", ctypes.c_int32)]
+                ("block_num", ctypes.c_int32), ("sm_count", ctypes.c_int32), ("tile_variant", ctypes.c_int32),
+                ("raster_group", ctypes.c_int32), ("l2_policy", ctypes.c_int32)]
 
 
 class PhasePlan(ctypes.Structure):
@@ -114,6 +116,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             "ffn_b200_reset": ([vp, vp], i32),
             "ffn_b200_set_wait_limit": ([vp, u64], i32),
             "ffn_b200_set_fault_injection": ([vp, i32], i32),
+            "ffn_b200_set_trace": ([vp, vp], i32),
             "ffn_b200_get_plan": ([vp, ctypes.POINTER(PlanInfo)], i32),
             "ffn_b200_destroy": ([vp], i32),
             "ffn_b200_launch": ([ctypes.POINTER(Problem), ctypes.POINTER(Buffers), vp], i32),

@@ -99,6 +99,33 @@ class PreparedFFN:
         if rc != _lib.OK:
             raise ValueError(f"set_fault_injection: {_lib.strerror(rc)}")
 
+    def trace(self):
+        """Runs once with per-CTA %globaltimer stamps and returns a dict of phase times (us)
+        relative to the earliest setup stamp: per-slot min/median/max over CTAs."""
+        import torch
+
+        grid = self.plan.block_num
+        stamps = torch.zeros((grid, 8), dtype=torch.int64, device=self.storage[0].device)
+        lib = _lib.load()
+        if lib.ffn_b200_set_trace(self.handle, stamps.data_ptr()) != _lib.OK:
+            raise RuntimeError("ffn_b200_set_trace failed")
+        try:
+            self.run()
+            self.check()
+        finally:
+            lib.ffn_b200_set_trace(self.handle, None)
+        t = stamps.cpu()
+        t0 = int(t[:, 0][t[:, 0] > 0].min())
+        names = ("start", "first_load", "down_ready", "last_load", "last_mma", "up_stored", "first_down", "end")
+        out = {}
+        for i, name in enumerate(names):
+            col = t[:, i][t[:, i] > 0].double()
+            if col.numel():
+                rel = (col - t0) / 1e3
+                out[name] = {"min": float(rel.min()), "median": float(rel.median()), "max": float(rel.max()),
+                             "ctas": int(col.numel())}
+        return out
+
     def close(self):
         if self.handle is not None:
             _lib.load().ffn_b200_destroy(self.handle)
@@ -121,14 +148,15 @@ def _map_prepare_error(rc):
 
 
 def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", block_num=None,
-                layout="linear", gelu="rational", tile=None):
+                layout="linear", gelu="rational", tile=None, raster_group=None, l2_policy=None):
     """Validates, plans and prepares storage and the launch handle without launching the FFN
     (reference ops/api.py:48-89).
 
     ``block_num`` is the persistent CTA count, at most the device's SM count (default: all
     SMs).  ``gelu`` selects the epilogue GELU: 'rational' (the reference kernel's clipped
     rational erf) or 'erf' (CUDA ``erff``).  ``tile`` forces a kernel variant (see
-    ``make_plan``); None chooses automatically.  Storage copies are device work timed
+    ``make_plan``); None chooses automatically; ``raster_group`` and ``l2_policy`` are
+    tuning overrides passed to ``make_plan``.  Storage copies are device work timed
     separately as ``preparation['auxiliary_device_interval_ms']``.
     """
     import torch
@@ -140,7 +168,8 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
     except (OSError, RuntimeError) as exc:
         raise KernelCompilationError(f"{type(exc).__name__}: {exc}") from exc
     props = torch.cuda.get_device_properties(x.device)
-    plan = make_plan(p, selection, block_num, gelu=gelu, sm_count=props.multi_processor_count, tile=tile)
+    plan = make_plan(p, selection, block_num, gelu=gelu, sm_count=props.multi_processor_count, tile=tile,
+                     raster_group=raster_group, l2_policy=l2_policy)
     if (props.major, props.minor) != (10, 0):
         raise RuntimeError("This implementation targets B200 (sm_100) only")
     if plan.block_num > props.multi_processor_count:
@@ -159,7 +188,8 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
                             counters.data_ptr(), flags.data_ptr(), status.data_ptr())
         prob = _lib.Problem(p.m, p.k, p.h, p.n, _lib.DTYPES[p.dtype], _lib.DOWN_IMPL_CODES[down_impl],
                             _lib.GELU_CODES[gelu], plan.block_num, props.multi_processor_count,
-                            _lib.TILE_VARIANTS[tile] if tile else 0)
+                            _lib.TILE_VARIANTS[tile] if tile else 0, int(raster_group or 0),
+                            _lib.L2_POLICIES[l2_policy] if l2_policy else 0)
         handle = ctypes.c_void_p()
         before = perf_counter()
         rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), x.device.index or 0, ctypes.byref(handle))

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -75,7 +76,7 @@ struct PhaseInput {
 // Fills one phase's schedule.  split=true applies the Stream-K tail split of the reference
 // (ops/kernel/ffn.py:642-665): sk = T mod C tail tiles, their sk*L k-blocks spread as
 // q = floor(sk*L / C) per CTA with the first (sk*L mod C) CTAs taking one more.
-int phase_plan(const PhaseInput& in, int tile_m, int bn, int C, bool split, ffn_b200_phase_plan* out) {
+int phase_plan(const PhaseInput& in, int tile_m, int bn, int C, bool split, int group, ffn_b200_phase_plan* out) {
   const int64_t tr = cdiv(in.rows, tile_m);
   const int64_t tq = cdiv(in.cols, bn);
   const int64_t T = tr * tq;
@@ -85,7 +86,7 @@ int phase_plan(const PhaseInput& in, int tile_m, int bn, int C, bool split, ffn_
   out->tiles_q = static_cast<int32_t>(tq);
   out->tiles = static_cast<int32_t>(T);
   out->k_blocks = static_cast<int32_t>(L);
-  out->group = static_cast<int32_t>(tr < 16 ? tr : 16);
+  out->group = static_cast<int32_t>(group < 1 ? 1 : (group > tr ? tr : group));
   if (split) {
     const int64_t sk = T % C;
     const int64_t iters = sk * L;
@@ -203,6 +204,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   const int grid = pr->block_num > 0 ? pr->block_num : sm;
   if (grid < 1 || grid > 65535 || pr->block_num < 0) return FFN_B200_ERR_INVALID;
   if (pr->tile_variant < 0 || pr->tile_variant > kNumVariants) return FFN_B200_ERR_INVALID;
+  if (pr->raster_group < 0 || pr->l2_policy < 0 || pr->l2_policy > 2) return FFN_B200_ERR_INVALID;
 
   std::memset(out, 0, sizeof(*out));
   int variant;
@@ -224,20 +226,35 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   const int C = grid / ncta;  // work-list owners (CTAs, or CTA pairs)
   const PhaseInput up = v.swap ? PhaseInput{pr->h, pr->m, pr->k} : PhaseInput{pr->m, pr->h, pr->k};
   const PhaseInput dn = v.swap ? PhaseInput{pr->n, pr->m, pr->h} : PhaseInput{pr->m, pr->n, pr->h};
+  // Raster group: a wave of C concurrent tiles spans `group` tile rows x C/group tile columns;
+  // balancing their operand bytes (group*tile_m = (C/group)*tile_n) minimises the K-slices a
+  // wave pulls through L2.
+  int group = pr->raster_group;
+  if (group <= 0) {
+    const double balanced = std::sqrt(static_cast<double>(C) * v.bn / tile_m);
+    group = static_cast<int>(std::lround(balanced));
+    // Prefer a nearby divisor of the tile-row count so no group is a ragged remainder
+    // (measured on cfg5: 16 rows of 128 beat 17 by 2 %).
+    const int64_t rows = cdiv(v.swap ? pr->h : pr->m, tile_m);
+    for (int d = 0; d <= static_cast<int>(0.3 * balanced); ++d) {
+      if (group - d >= 1 && rows % (group - d) == 0) { group -= d; break; }
+      if (rows % (group + d) == 0) { group += d; break; }
+    }
+  }
 
   // Up phase: data-parallel, with the tail wave split along K when whole tiles would leave
   // more than a tenth of the CTAs idle in the last wave (a schedule choice only).
   ffn_b200_phase_plan probe;
-  int rc = phase_plan(up, tile_m, v.bn, C, false, &probe);
+  int rc = phase_plan(up, tile_m, v.bn, C, false, group, &probe);
   if (rc) return rc;
   const int64_t waves = cdiv(probe.tiles, C);
   const bool up_split = (probe.tiles % C) != 0 && probe.k_blocks >= 2 &&
                         static_cast<double>(probe.tiles) < 0.9 * static_cast<double>(waves * C);
-  rc = phase_plan(up, tile_m, v.bn, C, up_split, &out->up);
+  rc = phase_plan(up, tile_m, v.bn, C, up_split, group, &out->up);
   if (rc) return rc;
 
   const bool streamk = pr->down_impl == FFN_B200_DOWN_STREAMK;
-  rc = phase_plan(dn, tile_m, v.bn, C, streamk, &out->down);
+  rc = phase_plan(dn, tile_m, v.bn, C, streamk, group, &out->down);
   if (rc) return rc;
   if (streamk && (out->down.tiles % C == 0 || out->down.k_blocks < 2)) return FFN_B200_ERR_NOT_APPLICABLE;
   if (static_cast<int64_t>(out->up.sk_tiles) * out->up.k_blocks >= (int64_t(1) << 31) ||
@@ -349,6 +366,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.C = plan.block_num / ncta;
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
+  P.l2_hints = prob.l2_policy == 2 ? 1 : 0;
   // Readiness counters gain 4 * ncta * (up tiles per row block) per launch, flags 4 per launch.
   const int64_t per_blk = 4ll * ncta * (sw ? plan.up.tiles_r : plan.up.tiles_q);
   h->epoch_limit = static_cast<unsigned>(((int64_t(1) << 30) / (per_blk > 4 ? per_blk : 4)));
@@ -474,6 +492,13 @@ int ffn_b200_set_wait_limit(ffn_b200_handle* h, uint64_t ns) {
 int ffn_b200_set_fault_injection(ffn_b200_handle* h, int mode) {
   if (!h || mode < 0 || mode > 1) return FFN_B200_ERR_INVALID;
   h->params.inject = mode;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_set_trace(ffn_b200_handle* h, uint64_t* device_stamps) {
+  if (!h) return FFN_B200_ERR_INVALID;
+  if (device_stamps && (reinterpret_cast<uintptr_t>(device_stamps) & 7u)) return FFN_B200_ERR_ALIGNMENT;
+  h->params.trace = reinterpret_cast<unsigned long long*>(device_stamps);
   return FFN_B200_OK;
 }
 

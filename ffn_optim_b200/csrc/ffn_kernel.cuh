@@ -77,6 +77,20 @@ struct Params {
   unsigned epoch;
   unsigned long long wait_limit_ns;
   int inject;
+  int l2_hints;          // 1: evict-last on A (row operand), evict-first on B (column operand)
+  unsigned long long* trace;  // optional [grid][8] %globaltimer stamps (see TraceSlot), null = off
+};
+
+// Per-CTA trace stamps (ns, %globaltimer) written when Params::trace is set.
+enum TraceSlot : int {
+  kTrStart = 0,       // setup done (barriers, TMEM)
+  kTrFirstLoad = 1,   // producer issued its first TMA load
+  kTrDownReady = 2,   // producer saw its first down tile's hidden rows ready
+  kTrLastLoad = 3,    // producer issued its last load
+  kTrLastMma = 4,     // MMA thread committed its last accumulator
+  kTrUpStored = 5,    // first epilogue warp finished its last up-phase unit
+  kTrFirstDown = 6,   // first epilogue warp got its first down-phase accumulator
+  kTrEnd = 7          // teardown reached
 };
 
 // ------------------------------------------------------------------------------------------
@@ -150,6 +164,24 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm,
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(bar)
       : "memory");
 }
+// Same with an L2 eviction-priority policy (from createpolicy).
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* tm, int c0, int c1, uint32_t bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, uint32_t src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
                ::"l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(src)
@@ -209,6 +241,14 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
+                                                      uint32_t cluster_bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(cluster_bar), "l"(policy)
       : "memory");
 }
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
@@ -400,6 +440,10 @@ __device__ __forceinline__ bool get_unit(const Params& p, int c, int idx, Unit& 
   return false;
 }
 
+__device__ __forceinline__ void trace_mark(const Params& p, int slot) {
+  if (p.trace) p.trace[static_cast<size_t>(blockIdx.x) * 8 + slot] = gtimer();
+}
+
 __device__ __forceinline__ void report(const Params& p, int code, int aux) {
   if (atomicCAS(p.status, 0, code) == 0) {
     p.status[1] = static_cast<int>(blockIdx.x);
@@ -408,6 +452,9 @@ __device__ __forceinline__ void report(const Params& p, int code, int aux) {
 }
 
 // Bounded mbarrier wait.  Returns false when the CTA aborts (timeout here or elsewhere).
+// On-chip pipeline waits get twice the limit of the cross-CTA waits below: when a readiness
+// counter or Stream-K flag never arrives, that wait (the cause) expires and reports first,
+// not the pipeline stages stalled behind it.
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                          const Params& p, int aux) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -418,7 +465,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
     if (mbar_try_wait(bar, parity)) return true;
     if ((++n & 15u) == 0) {
       if (*abort_flag) return false;
-      if (gtimer() - t0 > p.wait_limit_ns) {
+      if (gtimer() - t0 > 2 * p.wait_limit_ns) {
         report(p, 1, aux);
         *abort_flag = 1;
         return false;
@@ -533,6 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
   if constexpr (PAIR) cluster_sync();  // peer barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) trace_mark(p, kTrStart);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -543,6 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       int ready_blk = -1;
       const unsigned per_blk = 4u * kNcta * static_cast<unsigned>(SWAP ? p.up.tiles_r : p.up.tiles_q);
       const unsigned target = p.epoch * per_blk + (p.inject ? 1u : 0u);
+      // Optional L2 policy (off by default: on cfg5 it raised DRAM reads from 62 GB to 430 GB).
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_first();
+      const bool hints = p.l2_hints != 0 && !SWAP;
       bool ok = true;
 #pragma unroll 1
       for (int idx = 0; ok; ++idx) {
@@ -553,44 +605,85 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
         tile_coords(s, u.tile, tr, tq);
         const CUtensorMap* ta = u.phase ? &p.tm_a_dn : &p.tm_a_up;
         const CUtensorMap* tb = u.phase ? &p.tm_b_dn : &p.tm_b_up;
+        const int arow = tr * kTileM + static_cast<int>(rank) * kBM;
+        const int brow = tq * BN + static_cast<int>(rank) * LY::kBRows;
+        // One operand load into stage `st` (which = 0: A, 1: B), with the chosen L2 policy.
+        auto load = [&](int which, int st, int kb) {
+          const uint32_t dst = which == 0 ? sA + st * kABytes : sB + st * LY::kBBytes;
+          const CUtensorMap* tm = which == 0 ? ta : tb;
+          const int row = which == 0 ? arow : brow;
+          if constexpr (PAIR) {
+            const uint32_t fb = map_to_rank(full_bar(st), 0);
+            if (hints) tma_load_2d_pair_hint(dst, tm, kb * kBK, row, fb, which == 0 ? pol_a : pol_b);
+            else tma_load_2d_pair(dst, tm, kb * kBK, row, fb);
+          } else {
+            if (hints) tma_load_2d_hint(dst, tm, kb * kBK, row, full_bar(st), which == 0 ? pol_a : pol_b);
+            else tma_load_2d(dst, tm, kb * kBK, row, full_bar(st));
+          }
+        };
+        auto arm = [&](int st) {  // expect both operands' bytes of this stage
+          if constexpr (PAIR) {
+            if (leader) mbar_expect_tx(full_bar(st), kNcta * LY::kStageBytes);
+          } else {
+            mbar_expect_tx(full_bar(st), LY::kStageBytes);
+          }
+        };
+        int kb = u.kb0;
         if (u.phase == 1) {
           const int blk = SWAP ? tq : tr;
           if (blk != ready_blk) {
+            // The hidden rows of this tile are not known to be ready.  The weight operand
+            // (W2: A in swap mode, B otherwise) does not depend on them: fill up to STAGES
+            // ring slots with it, then wait for the rows and complete those stages with the
+            // hidden operand.  (An extra L2 prefetch of W2 here was measured neutral on the
+            // bandwidth-bound decode shape: it only moved bytes from the down to the up phase.)
+            const int wop = SWAP ? 0 : 1;
+            const int n_pre = min(STAGES, u.kb1 - u.kb0);
+            const int st0 = stage;
+            int pre = 0;
+            for (; pre < n_pre; ++pre) {
+              if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) { ok = false; break; }
+              arm(stage);
+              load(wop, stage, kb + pre);
+              if (issued == 0) trace_mark(p, kTrFirstLoad);
+              ++issued;
+              if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
             if (!wait_word_ge(p.counters + blk, target, abort_flag, p, 2, blk)) { ok = false; break; }
             fence_async_global();
+            if (ready_blk < 0) trace_mark(p, kTrDownReady);
             ready_blk = blk;
+            for (int j = 0; j < pre; ++j) load(1 - wop, (st0 + j) % STAGES, kb + j);
+            kb += pre;
           }
         }
-        const int arow = tr * kTileM + static_cast<int>(rank) * kBM;
-        const int brow = tq * BN + static_cast<int>(rank) * LY::kBRows;
 #pragma unroll 1
-        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+        for (; kb < u.kb1; ++kb) {
           if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) { ok = false; break; }
-          if constexpr (PAIR) {
-            const uint32_t fb = map_to_rank(full_bar(stage), 0);
-            if (leader) mbar_expect_tx(full_bar(stage), kNcta * LY::kStageBytes);
-            tma_load_2d_pair(sA + stage * kABytes, ta, kb * kBK, arow, fb);
-            tma_load_2d_pair(sB + stage * LY::kBBytes, tb, kb * kBK, brow, fb);
-          } else {
-            mbar_expect_tx(full_bar(stage), LY::kStageBytes);
-            tma_load_2d(sA + stage * kABytes, ta, kb * kBK, arow, full_bar(stage));
-            tma_load_2d(sB + stage * LY::kBBytes, tb, kb * kBK, brow, full_bar(stage));
-          }
+          arm(stage);
+          load(0, stage, kb);
+          load(1, stage, kb);
+          if (issued == 0) trace_mark(p, kTrFirstLoad);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
+      trace_mark(p, kTrLastLoad);
       // Drain: every issued load must land before the CTA may exit.  In a pair the
       // transaction bytes land on the leader's barriers, so the leader drains for both.
+      // One deadline for the whole drain: after an abort, stages armed for both operands
+      // but given only the weight operand never complete, and must not each wait the limit.
       if (leader) {
         const long long first = issued > STAGES ? issued - STAGES : 0;
+        const uint64_t t0 = gtimer();
+        bool late = false;
 #pragma unroll 1
-        for (long long i = first; i < issued; ++i) {
+        for (long long i = first; i < issued && !late; ++i) {
           const int s = static_cast<int>(i % STAGES);
           const uint32_t par = static_cast<uint32_t>((i / STAGES) & 1);
-          const uint64_t t0 = gtimer();
           while (!mbar_try_wait(full_bar(s), par)) {
-            if (gtimer() - t0 > p.wait_limit_ns) break;
+            if (gtimer() - t0 > p.wait_limit_ns) { late = true; break; }
           }
         }
       }
@@ -638,6 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
         }
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
+      trace_mark(p, kTrLastMma);
       // Drain: all issued MMAs complete before TMEM is released.
       if constexpr (PAIR) umma_commit_pair(drain_bar);
       else umma_commit(drain_bar);
@@ -654,6 +748,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
+    bool seen_down = false;
 #pragma unroll 1
     for (int idx = 0;; ++idx) {
       Unit u;
@@ -666,6 +761,8 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
+      if (ew == 0 && lane == 0 && u.phase == 1 && !seen_down) trace_mark(p, kTrFirstDown);
+      if (u.phase == 1) seen_down = true;
       // Stream-K owner: wait for every contributor's partial of this tile (same pair rank).
       if (u.role == kRoleOwner && u.c_first <= u.c_last) {
         if (lane == 0) {
@@ -802,6 +899,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
           __syncwarp();
           if (lane == 0) red_release_add(p.counters + blk, 1u);
         }
+        if (ew == 0 && lane == 0) trace_mark(p, kTrUpStored);
       }
     }
     if constexpr (!SWAP) {
@@ -814,6 +912,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
   __syncthreads();
   if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal it
   tc_fence_after();
+  if (threadIdx.x == 0) trace_mark(p, kTrEnd);
   if (warp == 1) {
     if constexpr (PAIR) tmem_dealloc_pair(tmem_base, LY::kTmemCols);
     else tmem_dealloc(tmem_base, LY::kTmemCols);

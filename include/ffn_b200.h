@@ -80,8 +80,12 @@ typedef struct {
   int32_t gelu;        /* ffn_b200_gelu */
   int32_t block_num;   /* persistent CTA count; 0 = one per SM */
   int32_t sm_count;    /* SMs of the target device; 0 = query the current device */
-  int32_t tile_variant; /* 0 = automatic; 1 + variant id forces one kernel variant
+  /* Tuning overrides, 0 = automatic (benchmarks and tests use them): */
+  int32_t tile_variant; /* 1 + variant id forces one kernel variant
                            (1: 128x256, 2: 128x128, 3: swap 16, 4: swap 64, 5: CTA pair 256x256) */
+  int32_t raster_group; /* tile rows per raster group (default: balances A and B bytes per wave) */
+  int32_t l2_policy;    /* 1: no L2 eviction hints (default); 2: evict-last on the row operand and
+                           evict-first on the column operand (measured: far more DRAM traffic) */
 } ffn_b200_problem;
 
 /* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
@@ -161,6 +165,13 @@ FFN_B200_EXPORT int ffn_b200_set_wait_limit(ffn_b200_handle* handle, uint64_t na
 /* Test hook: 1 makes every down tile wait for one readiness signal too many, so the
  * bounded wait runs out and the kernel reports FFN_B200_KERNEL_DEP_TIMEOUT. */
 FFN_B200_EXPORT int ffn_b200_set_fault_injection(ffn_b200_handle* handle, int mode);
+
+/* Tracing: when `device_stamps` (a device uint64[block_num][8], or NULL to switch off) is
+ * set, every later run writes per-CTA %globaltimer stamps (ns): 0 setup done, 1 first TMA
+ * load, 2 first down tile's hidden rows ready, 3 last load, 4 last MMA commit, 5 last up
+ * tile stored, 6 first down accumulator in the epilogue, 7 end.  Reference counterpart:
+ * the separate profiler pass of performance/collect.py:38-72. */
+FFN_B200_EXPORT int ffn_b200_set_trace(ffn_b200_handle* handle, uint64_t* device_stamps);
 
 FFN_B200_EXPORT int ffn_b200_get_plan(const ffn_b200_handle* handle, ffn_b200_plan* plan);
 FFN_B200_EXPORT int ffn_b200_destroy(ffn_b200_handle* handle);
