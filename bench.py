@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--flush", choices=("auto", "on", "off"), default="auto",
                     help="flush L2 between timed steps (auto: when the operands fit in 2x L2)")
+    ap.add_argument("--e2e-chunks", type=int, default=8)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
@@ -319,22 +320,22 @@ def main():
     e2e = None
     if world == 1 and not args.no_e2e:
         xh = x.cpu().pin_memory()
-        yh = torch.empty((p.m, p.n), dtype=x.dtype, pin_memory=True)
+        yh = torch.empty(p.output_shape, dtype=x.dtype, pin_memory=True)
+        chunks = args.e2e_chunks
         for _ in range(2):
-            y = runner.run(xh)
-            yh.copy_(y.reshape(p.m, p.n), non_blocking=True)
+            runner.run_host(xh, yh, chunks=chunks)
         torch.cuda.synchronize()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
         for _ in range(args.steps):
-            y = runner.run(xh)
-            yh.copy_(y.reshape(p.m, p.n), non_blocking=True)
+            runner.run_host(xh, yh, chunks=chunks)
         e2.record()
         e2.synchronize()
         ms2 = s2.elapsed_time(e2)
         check()
         e2e = {"value": fl * args.steps / (ms2 / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms2 / args.steps,
-               "h2d_bytes_per_step": p.m * p.k * x.element_size(), "d2h_bytes_per_step": p.m * p.n * x.element_size()}
+               "h2d_bytes_per_step": p.m * p.k * x.element_size(), "d2h_bytes_per_step": p.m * p.n * x.element_size(),
+               "api": f"PreparedFFN.run_host(pinned X, pinned Y, chunks={chunks})", "gpu_launches": chunks * args.steps}
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:

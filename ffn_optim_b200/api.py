@@ -67,14 +67,124 @@ class PreparedFFN:
                 raise RuntimeError(f"ffn_b200_run: {_lib.strerror(rc)}")
         return self._output_view()
 
+    def _chunk_handles(self, chunks):
+        """Launch handles for M-chunks of this FFN (rows rounded to 128), sharing its storage:
+        chunk c reads X rows [lo, hi), writes the same rows of hidden and Y, and has its own
+        readiness counters; the fp32 Stream-K workspace is shared (chunks run in order on
+        the preparation stream)."""
+        import torch
+
+        cached = getattr(self, "_chunks", None)
+        if cached is not None and cached[0] == chunks:
+            return cached[1]
+        p = self.plan.problem
+        rows = -(-p.m // chunks)
+        rows = -(-rows // 128) * 128
+        x2d, w1, w2, hidden, out, ws = self.storage[:6]
+        lib = _lib.load()
+        dev = x2d.device
+        handles = []
+        lo = 0
+        while lo < p.m:
+            hi = min(p.m, lo + rows)
+            sub = self.plan.problem.__class__((hi - lo, p.k), hi - lo, p.k, p.h, p.n, p.dtype, p.layout)
+            from .host.tiling import make_plan
+
+            o = self.plan.kernel.get("overrides", {})
+            plan = make_plan(sub, self.plan.selection, self.plan.block_num, gelu=self.plan.gelu,
+                             sm_count=torch.cuda.get_device_properties(dev).multi_processor_count,
+                             tile=o.get("tile"), raster_group=o.get("raster_group"), l2_policy=o.get("l2_policy"))
+            k = plan.kernel
+            if k["workspace_floats"] > ws.numel():
+                ws = torch.empty(int(k["workspace_floats"]), dtype=torch.float32, device=dev)
+            sync = torch.zeros(int(k["counter_words"]) + int(k["flag_words"]) + 4, dtype=torch.int32, device=dev)
+            cnt, flg, st = sync[:k["counter_words"]], sync[k["counter_words"]:-4], sync[-4:]
+            bufs = _lib.Buffers(x2d[lo].data_ptr(), x2d.stride(0), w1.data_ptr(), w1.stride(0), w2.data_ptr(),
+                                w2.stride(0), hidden[lo].data_ptr(), hidden.stride(0), out[lo].data_ptr(),
+                                out.stride(0), ws.data_ptr(), cnt.data_ptr(), flg.data_ptr(), st.data_ptr())
+            prob = _lib.Problem(hi - lo, p.k, p.h, p.n, _lib.DTYPES[p.dtype],
+                                _lib.DOWN_IMPL_CODES[self.plan.selection.down_impl], _lib.GELU_CODES[self.plan.gelu],
+                                plan.block_num, torch.cuda.get_device_properties(dev).multi_processor_count,
+                                _lib.TILE_VARIANTS[o["tile"]] if o.get("tile") else 0, int(o.get("raster_group") or 0),
+                                _lib.L2_POLICIES[o["l2_policy"]] if o.get("l2_policy") else 0)
+            h = ctypes.c_void_p()
+            rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), dev.index or 0, ctypes.byref(h))
+            if rc != _lib.OK:
+                raise _map_prepare_error(rc)
+            handles.append((lo, hi, h, (ws, sync)))
+            lo = hi
+        self._chunks = (chunks, handles)
+        self._chunk_streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        self._chunk_events = {}
+        return handles
+
+    def run_host(self, x_host, y_host, chunks=8):
+        """FFN from host memory to host memory with the copies overlapped.
+
+        ``x_host`` (``x.shape``) and ``y_host`` (``(*x.shape[:-1], N)``) are CPU tensors, pinned
+        for asynchronous copies.  M is split into ``chunks`` row ranges; chunk c's host->device
+        copy, fused kernel and device->host copy run on three streams so transfers overlap the
+        other chunks' kernels.  Returns ``y_host``; like :meth:`run` it is asynchronous: the
+        preparation stream waits for the last copy, so synchronising it (or :meth:`check`)
+        completes the call.
+        """
+        import torch
+
+        p = self.plan.problem
+        if tuple(x_host.shape) != tuple(p.input_shape) or tuple(y_host.shape) != tuple(p.output_shape):
+            raise ValueError("run_host: x_host / y_host must have the input / output shapes")
+        if x_host.dtype != self.storage[0].dtype or y_host.dtype != self.storage[0].dtype:
+            raise ValueError("run_host: host buffers must have the prepared dtype")
+        handles = self._chunk_handles(chunks)
+        h2d, d2h = self._chunk_streams
+        lib = _lib.load()
+        x2d, out = self.storage[0], self.storage[4]
+        xs, ys = x_host.reshape(p.m, p.k), y_host.reshape(p.m, p.n)
+        ev = self._chunk_events
+        with torch.cuda.device(x2d.device):
+            if torch.cuda.current_stream() != self.stream:
+                raise RuntimeError("PreparedFFN must run on its preparation stream; concurrent reuse is unsupported")
+            for lo, hi, h, _ in handles:
+                key = lo
+                done_k, done_out = ev.get(("k", key)), ev.get(("o", key))
+                with torch.cuda.stream(h2d):
+                    if done_k is not None:
+                        h2d.wait_event(done_k)  # the previous kernel of this chunk has read X
+                    x2d[lo:hi, :p.k].copy_(xs[lo:hi], non_blocking=True)
+                    e_in = torch.cuda.Event()
+                    e_in.record(h2d)
+                self.stream.wait_event(e_in)
+                if done_out is not None:
+                    self.stream.wait_event(done_out)  # the previous copy-out of these Y rows finished
+                rc = lib.ffn_b200_run(h, ctypes.c_void_p(self.stream.cuda_stream))
+                if rc != _lib.OK:
+                    raise RuntimeError(f"ffn_b200_run: {_lib.strerror(rc)}")
+                e_k = torch.cuda.Event()
+                e_k.record(self.stream)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(e_k)
+                    ys[lo:hi].copy_(out[lo:hi, :p.n], non_blocking=True)
+                    e_o = torch.cuda.Event()
+                    e_o.record(d2h)
+                ev[("k", key)], ev[("o", key)] = e_k, e_o
+            for lo, _, _, _ in handles:
+                self.stream.wait_event(ev[("o", lo)])
+        return y_host
+
     def status(self):
         """Synchronises the stream and returns the kernel's status words [code, cta, aux, 0]."""
         self.stream.synchronize()
         return [int(v) for v in self.storage[8].tolist()]
 
     def check(self):
-        """Raises RuntimeError if any launch since the last reset reported a device error."""
+        """Raises RuntimeError if any launch since the last reset reported a device error
+        (including the chunk launches of :meth:`run_host`)."""
         st = self.status()
+        for _, _, _, (_, sync) in (getattr(self, "_chunks", None) or (0, []))[1]:
+            cst = [int(v) for v in sync[-4:].tolist()]
+            if cst[0] != 0:
+                st = cst
+                break
         if st[0] != 0:
             self.reset()
             msg = _lib.KERNEL_ERRORS.get(st[0], f"error {st[0]}")
@@ -130,6 +240,9 @@ class PreparedFFN:
         if self.handle is not None:
             _lib.load().ffn_b200_destroy(self.handle)
             self.handle = None
+        for _, _, h, _ in (getattr(self, "_chunks", None) or (0, []))[1]:
+            _lib.load().ffn_b200_destroy(h)
+        self._chunks = None
 
     def __del__(self):
         try:

@@ -29,36 +29,44 @@ using KernelFn = void (*)(const Params);
 struct Variant {
   int bn, stages;
   bool swap, pair;
+  int ksub;  // 64-wide K sub-blocks per pipeline stage
 };
 // 0: prefill tiles 128x256 (one CTA), 1: 128x128 for small grids, 2/3: swap-AB decode
-// tiles (16 / 64 tokens), 4: prefill tiles 256x256 computed by a CTA pair (cta_group::2).
-constexpr Variant kVariants[] = {{256, 4, false, false}, {128, 6, false, false}, {16, 8, true, false},
-                                 {64, 8, true, false}, {256, 6, false, true}};
-constexpr int kNumVariants = 5;
+// tiles (16 / 64 tokens), 4: prefill tiles 256x256 computed by a CTA pair (cta_group::2),
+// 5/6: swap-AB decode tiles with 256-wide K stages (longer contiguous weight reads).
+constexpr Variant kVariants[] = {{256, 4, false, false, 1}, {128, 6, false, false, 1}, {16, 8, true, false, 1},
+                                 {64, 8, true, false, 1},   {256, 6, false, true, 1},  {16, 3, true, false, 4},
+                                 {64, 4, true, false, 2}};
+constexpr int kNumVariants = 7;
 
-template <int BN, int ST, bool SW, bool PR>
+template <int BN, int ST, bool SW, bool PR, int KS>
 KernelFn pick_kernel(int bf16, int gelu) {
   using namespace ffnb200;
-  if (bf16) return gelu ? ffn_fused_kernel<BN, ST, SW, PR, true, 1> : ffn_fused_kernel<BN, ST, SW, PR, true, 0>;
-  return gelu ? ffn_fused_kernel<BN, ST, SW, PR, false, 1> : ffn_fused_kernel<BN, ST, SW, PR, false, 0>;
+  if (bf16)
+    return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, true, 1> : ffn_fused_kernel<BN, ST, SW, PR, KS, true, 0>;
+  return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, false, 1> : ffn_fused_kernel<BN, ST, SW, PR, KS, false, 0>;
 }
 KernelFn kernel_for(int variant, int bf16, int gelu) {
   switch (variant) {
-    case 0: return pick_kernel<256, 4, false, false>(bf16, gelu);
-    case 1: return pick_kernel<128, 6, false, false>(bf16, gelu);
-    case 2: return pick_kernel<16, 8, true, false>(bf16, gelu);
-    case 3: return pick_kernel<64, 8, true, false>(bf16, gelu);
-    case 4: return pick_kernel<256, 6, false, true>(bf16, gelu);
+    case 0: return pick_kernel<256, 4, false, false, 1>(bf16, gelu);
+    case 1: return pick_kernel<128, 6, false, false, 1>(bf16, gelu);
+    case 2: return pick_kernel<16, 8, true, false, 1>(bf16, gelu);
+    case 3: return pick_kernel<64, 8, true, false, 1>(bf16, gelu);
+    case 4: return pick_kernel<256, 6, false, true, 1>(bf16, gelu);
+    case 5: return pick_kernel<16, 3, true, false, 4>(bf16, gelu);
+    case 6: return pick_kernel<64, 4, true, false, 2>(bf16, gelu);
   }
   return nullptr;
 }
 int smem_for(int variant) {
   switch (variant) {
-    case 0: return ffnb200::Layout<256, 4, false, false>::kSmem;
-    case 1: return ffnb200::Layout<128, 6, false, false>::kSmem;
-    case 2: return ffnb200::Layout<16, 8, true, false>::kSmem;
-    case 3: return ffnb200::Layout<64, 8, true, false>::kSmem;
-    case 4: return ffnb200::Layout<256, 6, false, true>::kSmem;
+    case 0: return ffnb200::Layout<256, 4, false, false, 1>::kSmem;
+    case 1: return ffnb200::Layout<128, 6, false, false, 1>::kSmem;
+    case 2: return ffnb200::Layout<16, 8, true, false, 1>::kSmem;
+    case 3: return ffnb200::Layout<64, 8, true, false, 1>::kSmem;
+    case 4: return ffnb200::Layout<256, 6, false, true, 1>::kSmem;
+    case 5: return ffnb200::Layout<16, 3, true, false, 4>::kSmem;
+    case 6: return ffnb200::Layout<64, 4, true, false, 2>::kSmem;
   }
   return 0;
 }
@@ -76,11 +84,12 @@ struct PhaseInput {
 // Fills one phase's schedule.  split=true applies the Stream-K tail split of the reference
 // (ops/kernel/ffn.py:642-665): sk = T mod C tail tiles, their sk*L k-blocks spread as
 // q = floor(sk*L / C) per CTA with the first (sk*L mod C) CTAs taking one more.
-int phase_plan(const PhaseInput& in, int tile_m, int bn, int C, bool split, int group, ffn_b200_phase_plan* out) {
+int phase_plan(const PhaseInput& in, int tile_m, int bn, int tile_k, int C, bool split, int group,
+               ffn_b200_phase_plan* out) {
   const int64_t tr = cdiv(in.rows, tile_m);
   const int64_t tq = cdiv(in.cols, bn);
   const int64_t T = tr * tq;
-  const int64_t L = cdiv(in.depth, ffnb200::kBK);
+  const int64_t L = cdiv(in.depth, tile_k);
   if (T >= (int64_t(1) << 31) || tr >= (int64_t(1) << 31)) return FFN_B200_ERR_TOO_LARGE;
   out->tiles_r = static_cast<int32_t>(tr);
   out->tiles_q = static_cast<int32_t>(tq);
@@ -245,16 +254,17 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   // Up phase: data-parallel, with the tail wave split along K when whole tiles would leave
   // more than a tenth of the CTAs idle in the last wave (a schedule choice only).
   ffn_b200_phase_plan probe;
-  int rc = phase_plan(up, tile_m, v.bn, C, false, group, &probe);
+  const int tile_k = ffnb200::kBK * v.ksub;
+  int rc = phase_plan(up, tile_m, v.bn, tile_k, C, false, group, &probe);
   if (rc) return rc;
   const int64_t waves = cdiv(probe.tiles, C);
   const bool up_split = (probe.tiles % C) != 0 && probe.k_blocks >= 2 &&
                         static_cast<double>(probe.tiles) < 0.9 * static_cast<double>(waves * C);
-  rc = phase_plan(up, tile_m, v.bn, C, up_split, group, &out->up);
+  rc = phase_plan(up, tile_m, v.bn, tile_k, C, up_split, group, &out->up);
   if (rc) return rc;
 
   const bool streamk = pr->down_impl == FFN_B200_DOWN_STREAMK;
-  rc = phase_plan(dn, tile_m, v.bn, C, streamk, group, &out->down);
+  rc = phase_plan(dn, tile_m, v.bn, tile_k, C, streamk, group, &out->down);
   if (rc) return rc;
   if (streamk && (out->down.tiles % C == 0 || out->down.k_blocks < 2)) return FFN_B200_ERR_NOT_APPLICABLE;
   if (static_cast<int64_t>(out->up.sk_tiles) * out->up.k_blocks >= (int64_t(1) << 31) ||
@@ -266,7 +276,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   out->cta_pair = v.pair ? 1 : 0;
   out->tile_m = tile_m;
   out->tile_n = v.bn;
-  out->tile_k = ffnb200::kBK;
+  out->tile_k = tile_k;
   out->stages = v.stages;
   out->block_num = C * ncta;
   out->tmem_cols = tmem_cols_for(variant);

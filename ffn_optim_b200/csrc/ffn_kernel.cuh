@@ -494,17 +494,19 @@ __device__ __forceinline__ bool wait_word_ge(const unsigned* word, unsigned targ
 // ------------------------------------------------------------------------------------------
 // The kernel
 // ------------------------------------------------------------------------------------------
-template <int BN, int STAGES, bool SWAP, bool PAIR = false>
+template <int BN, int STAGES, bool SWAP, bool PAIR = false, int KSUB = 1>
 struct Layout {
   static constexpr int kNcta = PAIR ? 2 : 1;       // CTAs per tile (cluster size)
   static constexpr int kBRows = BN / kNcta;         // B rows each CTA loads per stage
-  static constexpr int kBBytes = kBRows * kBK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBSub = kBRows * kBK * 2;    // one 64-wide K sub-block of B
+  static constexpr int kAStage = KSUB * kABytes;    // a stage holds KSUB adjacent K sub-blocks
+  static constexpr int kBStage = KSUB * kBSub;
+  static constexpr int kStageBytes = kAStage + kBStage;
   static constexpr int kEpiBytes = SWAP ? 0 : 4 * 2 * kStageBufBytes;
   static constexpr int kBarBytes = 256;
   static constexpr int kSmem = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiBytes + kBarBytes;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static_assert((kBBytes % 1024) == 0, "B tile must be whole swizzle atoms");
+  static_assert((kBSub % 1024) == 0, "B tile must be whole swizzle atoms");
   static_assert((2 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");
   static_assert(!PAIR || !SWAP, "CTA pairs are used for prefill tiles only");
 };
@@ -515,9 +517,9 @@ struct Layout {
 // barrier; the leader's MMA thread issues the pair MMAs, whose D lands 128 rows in each
 // CTA's TMEM, and its tcgen05.commit arrives on the empty / tmem-full barriers of both CTAs;
 // each CTA's epilogue stores its own 128 rows and releases the accumulator on the leader.
-template <int BN, int STAGES, bool SWAP, bool PAIR, bool BF16, int GELU>
+template <int BN, int STAGES, bool SWAP, bool PAIR, int KSUB, bool BF16, int GELU>
 __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_constant__ Params p) {
-  using LY = Layout<BN, STAGES, SWAP, PAIR>;
+  using LY = Layout<BN, STAGES, SWAP, PAIR, KSUB>;
   constexpr int kNcta = LY::kNcta;
   constexpr int kTileM = kBM * kNcta;
   constexpr uint32_t kIdesc = make_idesc<BF16, BN, kTileM>();
@@ -529,8 +531,8 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t sA = base;
-  const uint32_t sB = sA + STAGES * kABytes;
-  const uint32_t sE = sB + STAGES * LY::kBBytes;
+  const uint32_t sB = sA + STAGES * LY::kAStage;
+  const uint32_t sE = sB + STAGES * LY::kBStage;
   const uint32_t sBar = sE + LY::kEpiBytes;
   auto full_bar = [&](int s) { return sBar + 8u * s; };
   auto empty_bar = [&](int s) { return sBar + 8u * (STAGES + s); };
@@ -609,16 +611,20 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
         const int brow = tq * BN + static_cast<int>(rank) * LY::kBRows;
         // One operand load into stage `st` (which = 0: A, 1: B), with the chosen L2 policy.
         auto load = [&](int which, int st, int kb) {
-          const uint32_t dst = which == 0 ? sA + st * kABytes : sB + st * LY::kBBytes;
           const CUtensorMap* tm = which == 0 ? ta : tb;
           const int row = which == 0 ? arow : brow;
-          if constexpr (PAIR) {
-            const uint32_t fb = map_to_rank(full_bar(st), 0);
-            if (hints) tma_load_2d_pair_hint(dst, tm, kb * kBK, row, fb, which == 0 ? pol_a : pol_b);
-            else tma_load_2d_pair(dst, tm, kb * kBK, row, fb);
-          } else {
-            if (hints) tma_load_2d_hint(dst, tm, kb * kBK, row, full_bar(st), which == 0 ? pol_a : pol_b);
-            else tma_load_2d(dst, tm, kb * kBK, row, full_bar(st));
+#pragma unroll
+          for (int j = 0; j < KSUB; ++j) {
+            const uint32_t dst = which == 0 ? sA + st * LY::kAStage + j * kABytes : sB + st * LY::kBStage + j * LY::kBSub;
+            const int kx = (kb * KSUB + j) * kBK;
+            if constexpr (PAIR) {
+              const uint32_t fb = map_to_rank(full_bar(st), 0);
+              if (hints) tma_load_2d_pair_hint(dst, tm, kx, row, fb, which == 0 ? pol_a : pol_b);
+              else tma_load_2d_pair(dst, tm, kx, row, fb);
+            } else {
+              if (hints) tma_load_2d_hint(dst, tm, kx, row, full_bar(st), which == 0 ? pol_a : pol_b);
+              else tma_load_2d(dst, tm, kx, row, full_bar(st));
+            }
           }
         };
         auto arm = [&](int st) {  // expect both operands' bytes of this stage
@@ -707,14 +713,17 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
         for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!wait_bar(full_bar(stage), phase, abort_flag, p, 300 + stage)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t da = sw128_desc(sA + stage * kABytes);
-          const uint64_t db = sw128_desc(sB + stage * LY::kBBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            // +32 bytes along K inside the 128-byte swizzle atom = +2 in the 16-byte address field
-            const uint32_t accum = (kb > u.kb0 || k > 0) ? 1u : 0u;
-            if constexpr (PAIR) umma_f16_pair(d, da + 2 * k, db + 2 * k, kIdesc, accum);
-            else umma_f16(d, da + 2 * k, db + 2 * k, kIdesc, accum);
+          for (int j = 0; j < KSUB; ++j) {
+            const uint64_t da = sw128_desc(sA + stage * LY::kAStage + j * kABytes);
+            const uint64_t db = sw128_desc(sB + stage * LY::kBStage + j * LY::kBSub);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              // +32 bytes along K inside the 128-byte swizzle atom = +2 in the 16-byte address field
+              const uint32_t accum = (kb > u.kb0 || j > 0 || k > 0) ? 1u : 0u;
+              if constexpr (PAIR) umma_f16_pair(d, da + 2 * k, db + 2 * k, kIdesc, accum);
+              else umma_f16(d, da + 2 * k, db + 2 * k, kIdesc, accum);
+            }
           }
           if constexpr (PAIR) {
             umma_commit_pair_both(empty_bar(stage));

@@ -82,7 +82,8 @@ typedef struct {
   int32_t sm_count;    /* SMs of the target device; 0 = query the current device */
   /* Tuning overrides, 0 = automatic (benchmarks and tests use them): */
   int32_t tile_variant; /* 1 + variant id forces one kernel variant
-                           (1: 128x256, 2: 128x128, 3: swap 16, 4: swap 64, 5: CTA pair 256x256) */
+                           (1: 128x256, 2: 128x128, 3: swap 16, 4: swap 64, 5: CTA pair 256x256,
+                            6: swap 16 with 256-wide K stages, 7: swap 64 with 128-wide K stages) */
   int32_t raster_group; /* tile rows per raster group (default: balances A and B bytes per wave) */
   int32_t l2_policy;    /* 1: no L2 eviction hints (default); 2: evict-last on the row operand and
                            evict-first on the column operand (measured: far more DRAM traffic) */
@@ -90,7 +91,7 @@ typedef struct {
 
 /* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
  * rows/cols are the tile grid of the MMA's A and B operands; k_blocks is the number of
- * 64-wide K steps per tile.  dp_tiles are computed whole by one CTA; the sk_tiles tail
+ * tile_k-wide K steps (pipeline stages) per tile.  dp_tiles are computed whole by one CTA; the sk_tiles tail
  * is split along K over all CTAs (Stream-K), sk_iters (+1 for the first sk_rem CTAs)
  * K steps per CTA. */
 typedef struct {

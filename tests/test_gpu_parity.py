@@ -208,3 +208,23 @@ def test_prepared_semantics():
     assert torch.equal(y3, ref)
     with pytest.raises(ValueError):
         prepare_ffn(x, w1, w2, block_num=10_000)
+
+
+@pytest.mark.parametrize("case_id,chunks", [("cfg1_fp16", 4), ("cfg2_bf16", 5), ("cfg3_bf16", 2)])
+def test_run_host_matches_run(case_id, chunks):
+    """Host-to-host path with overlapped copies equals the device path (ragged chunks, padded
+    pitches), twice in a row with different inputs."""
+    case = C.get_case(case_id)
+    p = C.case_problem(case)
+    x, w1, w2 = C.make_inputs(case, device="cuda")
+    prepared = prepare_ffn(x, w1, w2, down_impl=case["down_impl"])
+    xh = x.contiguous().cpu().pin_memory()
+    yh = torch.empty(p.output_shape, dtype=x.dtype, pin_memory=True)
+    for step in range(2):
+        if step:
+            xh.copy_((xh.float() * -0.5).to(x.dtype))
+        want = prepare_ffn(xh.cuda(), w1, w2, down_impl=case["down_impl"]).run().cpu()
+        prepared.run_host(xh, yh, chunks=chunks)
+        prepared.check()
+        dt = p.dtype
+        assert_close_bits(bits_of(yh.reshape(-1, p.n)), bits_of(want.reshape(-1, p.n)), dt)
