@@ -42,7 +42,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="cfg5_bf16")
-    ap.add_argument("--shard", choices=("h", "m"), default="h")
+    ap.add_argument("--shard", choices=("h", "hf", "m"), default="h",
+                    help="N>1: h = H-sharded + NCCL reduce-scatter, hf = H-sharded with the reduce-scatter "
+                         "fused into the kernel (NVLink peer stores), m = M-sharded")
     ap.add_argument("--chunks", type=int, default=4)
     ap.add_argument("--tile", default=None, help="force a kernel variant (see ffn_optim_b200._lib.TILE_VARIANTS)")
     ap.add_argument("--cpu-rows", type=int, default=1024)
@@ -252,6 +254,14 @@ def main():
         kernel_runs = lambda: runner.run()  # noqa: E731
         check = runner.check
         parallelism = "single"
+    elif args.shard == "hf":
+        from ffn_optim_b200.sharded import FusedTensorParallelFFN
+
+        runner = FusedTensorParallelFFN(x, w1, w2, down_impl=down)
+        launches = 1
+        kernel_runs = runner.run
+        check = runner.check
+        parallelism = f"tp-h{world} (reduce-scatter fused in the kernel, NVLink peer stores)"
     elif args.shard == "h":
         from ffn_optim_b200.sharded import TensorParallelFFN
 
@@ -347,12 +357,12 @@ def main():
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
                "sample": f"{rows} of {p.m} rows of {args.workload} (full weights), {sec:.1f} s, numpy float32 BLAS"}
 
-    first = runner if world == 1 else (runner.chunks[0].prepared if parallelism.startswith("tp") else runner.prepared)
+    first = runner if world == 1 else (runner.chunks[0].prepared if hasattr(runner, "chunks") else runner.prepared)
     block_num = first.plan.block_num
     variant = {v: k for k, v in _lib_variants().items()}.get(first.plan.kernel["variant"] + 1)
     burst, sustained, hbm, src = peaks()
     per_launch_ms = ms_step / launches
-    flops_launch = fl / world / launches if parallelism.startswith("tp") else fl / world
+    flops_launch = fl / world / launches
     achieved = flops_launch / (per_launch_ms / 1e3) / 1e12
     traffic = traffic_for(args.workload) if world == 1 else None
     roofline = {"bound": "tensor", "achieved": achieved, "peak": burst, "unit": "TFLOP/s", "frac": achieved / burst,

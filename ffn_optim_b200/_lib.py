@@ -32,13 +32,15 @@ TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pa
                  "swap16k4": 6, "swap64k2": 7}
 L2_POLICIES = {"none": 1, "stream_b": 2}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",
-                 3: "Stream-K partial wait timed out"}
+                 3: "Stream-K partial wait timed out", 4: "peer GPU partial wait timed out (fused reduce-scatter)"}
 
 # Every symbol the header declares; the CPU tests check the library exports all of them.
 EXPORTED = ("ffn_b200_abi_version", "ffn_b200_strerror", "ffn_b200_device_info", "ffn_b200_make_plan",
             "ffn_b200_prepare", "ffn_b200_run", "ffn_b200_rebind_io", "ffn_b200_reset",
             "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_set_trace", "ffn_b200_get_plan",
-            "ffn_b200_destroy", "ffn_b200_launch", "ffn_b200_run_noalloc")
+            "ffn_b200_destroy", "ffn_b200_launch", "ffn_b200_run_noalloc", "ffn_b200_peer_alloc",
+            "ffn_b200_peer_open", "ffn_b200_peer_close", "ffn_b200_peer_free", "ffn_b200_reduce_scatter_bytes",
+            "ffn_b200_set_reduce_scatter")
 
 
 class Problem(ctypes.Structure):
@@ -122,6 +124,12 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             "ffn_b200_destroy": ([vp], i32),
             "ffn_b200_launch": ([ctypes.POINTER(Problem), ctypes.POINTER(Buffers), vp], i32),
             "ffn_b200_run_noalloc": ([ctypes.POINTER(Problem), vp, i64, vp, i64, vp, i64, vp, i64, vp, vp], i32),
+            "ffn_b200_peer_alloc": ([u64, ctypes.POINTER(vp), vp], i32),
+            "ffn_b200_peer_open": ([vp, ctypes.POINTER(vp)], i32),
+            "ffn_b200_peer_close": ([vp], i32),
+            "ffn_b200_peer_free": ([vp], i32),
+            "ffn_b200_reduce_scatter_bytes": ([vp, i32, ctypes.POINTER(u64), ctypes.POINTER(u64)], i32),
+            "ffn_b200_set_reduce_scatter": ([vp, i32, i32, ctypes.POINTER(vp), ctypes.POINTER(vp), vp, i64], i32),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(lib, name)

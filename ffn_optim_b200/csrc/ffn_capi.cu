@@ -430,6 +430,14 @@ int ffn_b200_reset(ffn_b200_handle* h, void* stream) {
     cudaGetLastError();
     return FFN_B200_ERR_CUDA;
   }
+  if (h->params.rs_world > 1) {
+    const size_t band = static_cast<size_t>(h->params.rs_band_tiles) * h->plan.down.tiles_q;
+    if (cudaMemsetAsync(h->params.rs_flags[h->params.rs_rank], 0, 4 * band * h->params.rs_world, st) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return FFN_B200_ERR_CUDA;
+    }
+  }
   h->epoch = 0;
   return FFN_B200_OK;
 }
@@ -502,6 +510,89 @@ int ffn_b200_set_wait_limit(ffn_b200_handle* h, uint64_t ns) {
 int ffn_b200_set_fault_injection(ffn_b200_handle* h, int mode) {
   if (!h || mode < 0 || mode > 1) return FFN_B200_ERR_INVALID;
   h->params.inject = mode;
+  return FFN_B200_OK;
+}
+
+// ---- multi-GPU: peer-visible buffers and the fused reduce-scatter ----------------------
+int ffn_b200_peer_alloc(uint64_t bytes, void** dev_ptr, void* ipc_handle) {
+  if (!dev_ptr || !ipc_handle || bytes == 0) return FFN_B200_ERR_INVALID;
+  void* ptr = nullptr;
+  if (cudaMalloc(&ptr, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return FFN_B200_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t hd;
+  if (cudaMemset(ptr, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&hd, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(ptr);
+    return FFN_B200_ERR_CUDA;
+  }
+  std::memcpy(ipc_handle, &hd, sizeof(hd));
+  *dev_ptr = ptr;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_peer_open(const void* ipc_handle, void** dev_ptr) {
+  if (!ipc_handle || !dev_ptr) return FFN_B200_ERR_INVALID;
+  cudaIpcMemHandle_t hd;
+  std::memcpy(&hd, ipc_handle, sizeof(hd));
+  if (cudaIpcOpenMemHandle(dev_ptr, hd, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return FFN_B200_ERR_CUDA;
+  }
+  return FFN_B200_OK;
+}
+
+int ffn_b200_peer_close(void* dev_ptr) {
+  if (!dev_ptr) return FFN_B200_ERR_INVALID;
+  if (cudaIpcCloseMemHandle(dev_ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return FFN_B200_ERR_CUDA;
+  }
+  return FFN_B200_OK;
+}
+
+int ffn_b200_peer_free(void* dev_ptr) {
+  if (!dev_ptr) return FFN_B200_ERR_INVALID;
+  if (cudaFree(dev_ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return FFN_B200_ERR_CUDA;
+  }
+  return FFN_B200_OK;
+}
+
+int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* h, int world, uint64_t* stage_bytes, uint64_t* flag_bytes) {
+  if (!h || !stage_bytes || !flag_bytes || world < 2 || world > ffnb200::kMaxRanks) return FFN_B200_ERR_INVALID;
+  const ffn_b200_plan& pl = h->plan;
+  if (pl.swap_ab || pl.cta_pair || pl.down.tiles_r % world) return FFN_B200_ERR_INVALID;
+  const uint64_t band = static_cast<uint64_t>(pl.down.tiles_r / world) * pl.down.tiles_q;
+  *stage_bytes = 2ull * world * band * ffnb200::kBM * pl.tile_n * 2;
+  *flag_bytes = 4ull * world * band;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, void* const* stage_ptrs,
+                                void* const* flag_ptrs, void* y_local, int64_t ldy_local) {
+  if (!h || world < 2 || world > ffnb200::kMaxRanks || rank < 0 || rank >= world || !stage_ptrs || !flag_ptrs ||
+      !y_local)
+    return FFN_B200_ERR_INVALID;
+  const ffn_b200_plan& pl = h->plan;
+  if (pl.swap_ab || pl.cta_pair || pl.down.tiles_r % world) return FFN_B200_ERR_INVALID;
+  if (h->prob.m % (static_cast<int64_t>(world) * pl.tile_m) != 0) return FFN_B200_ERR_INVALID;
+  if (!aligned16(y_local) || ldy_local < h->prob.n || (ldy_local % 8) != 0) return FFN_B200_ERR_ALIGNMENT;
+  for (int r = 0; r < world; ++r)
+    if (!stage_ptrs[r] || !flag_ptrs[r] || !aligned16(stage_ptrs[r])) return FFN_B200_ERR_INVALID;
+  const int rc = encode_2d(&h->params.tm_st_y, y_local, h->prob.dtype, h->prob.n, h->prob.m / world, ldy_local, 64,
+                           ffnb200::kStoreRows);
+  if (rc) return rc;
+  Params& P = h->params;
+  P.rs_world = world;
+  P.rs_rank = rank;
+  P.rs_band_tiles = pl.down.tiles_r / world;
+  for (int r = 0; r < world; ++r) {
+    P.rs_stage[r] = static_cast<uint16_t*>(stage_ptrs[r]);
+    P.rs_flags[r] = static_cast<unsigned*>(flag_ptrs[r]);
+  }
   return FFN_B200_OK;
 }
 

@@ -48,6 +48,7 @@ constexpr int kEpiThreads = 128;  // warps 2..5
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kStoreRows = 32;    // rows per epilogue warp (one TMEM sub-partition)
 constexpr int kStageBufBytes = kStoreRows * 128;  // 32 rows x 64 x 16-bit, 128B-swizzled
+constexpr int kMaxRanks = 8;                      // GPUs of one fused reduce-scatter
 
 enum : int { kRoleFull = 0, kRoleOwner = 1, kRoleContrib = 2 };
 
@@ -79,6 +80,13 @@ struct Params {
   int inject;
   int l2_hints;          // 1: evict-last on A (row operand), evict-first on B (column operand)
   unsigned long long* trace;  // optional [grid][8] %globaltimer stamps (see TraceSlot), null = off
+  // Fused reduce-scatter of the down phase across `rs_world` GPUs (tensor parallel over H):
+  // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
+  // of another rank's band is pushed as a bf16 partial into that rank's staging buffer over
+  // NVLink; an owner sums the partials of its band in ascending rank order.
+  int rs_world, rs_rank, rs_band_tiles;
+  uint16_t* rs_stage[kMaxRanks];   // per rank: [2 parity][world][band tiles][kBM][BN] bf16
+  unsigned* rs_flags[kMaxRanks];   // per rank: [world][band tiles] push counts (4 per launch)
 };
 
 // Per-CTA trace stamps (ns, %globaltimer) written when Params::trace is set.
@@ -149,6 +157,14 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 }
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -369,6 +385,16 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 template <bool BF16>
+__device__ __forceinline__ float unpack_lo(uint32_t w) {
+  if constexpr (BF16) return __uint_as_float(w << 16);
+  else return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+}
+template <bool BF16>
+__device__ __forceinline__ float unpack_hi(uint32_t w) {
+  if constexpr (BF16) return __uint_as_float(w & 0xFFFF0000u);
+  else return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+}
+template <bool BF16>
 __device__ __forceinline__ uint16_t cvt1(float a) {
   if constexpr (BF16) {
     __nv_bfloat16 h = __float2bfloat16_rn(a);
@@ -406,6 +432,15 @@ __device__ __forceinline__ void tile_coords(const PhaseSched& s, int t, int& tr,
   tr = r0 + rem % gs;
   tq = rem / gs;
 }
+// Tile coordinates of a unit.  Under the fused reduce-scatter every rank visits the down
+// phase's bands of tile rows starting after its own band, so pushes to the other ranks go
+// out first and its own band, which waits for their partials, comes last.
+__device__ __forceinline__ void unit_coords(const Params& p, const Unit& u, int& tr, int& tq) {
+  const PhaseSched& s = u.phase ? p.dn : p.up;
+  tile_coords(s, u.tile, tr, tq);
+  if (u.phase == 1 && p.rs_world > 1) tr = (tr + (p.rs_rank + 1) * p.rs_band_tiles) % s.tiles_r;
+}
+
 __device__ __forceinline__ bool get_unit(const Params& p, int c, int idx, Unit& u) {
 #pragma unroll 1
   for (int ph = 0; ph < 2; ++ph) {
@@ -473,15 +508,18 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
     }
   }
 }
-// Bounded wait until *word >= target (wrapping compare).  Acquire at GPU scope.
+// Bounded wait until *word >= target (wrapping compare).  Acquire at GPU scope, or at
+// system scope (SYS) for words written by peer GPUs.
+template <bool SYS = false>
 __device__ __forceinline__ bool wait_word_ge(const unsigned* word, unsigned target, volatile int* abort_flag,
                                              const Params& p, int code, int aux) {
-  if (static_cast<int>(ld_acquire(word) - target) >= 0) return true;
+  auto load = [&]() { return SYS ? ld_acquire_sys(word) : ld_acquire(word); };
+  if (static_cast<int>(load() - target) >= 0) return true;
   const uint64_t t0 = gtimer();
 #pragma unroll 1
   while (true) {
     __nanosleep(64);
-    if (static_cast<int>(ld_acquire(word) - target) >= 0) return true;
+    if (static_cast<int>(load() - target) >= 0) return true;
     if (*abort_flag) return false;
     if (gtimer() - t0 > p.wait_limit_ns) {
       report(p, code, aux);
@@ -602,9 +640,8 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       for (int idx = 0; ok; ++idx) {
         Unit u;
         if (!get_unit(p, cta, idx, u)) break;
-        const PhaseSched& s = u.phase ? p.dn : p.up;
         int tr, tq;
-        tile_coords(s, u.tile, tr, tq);
+        unit_coords(p, u, tr, tq);
         const CUtensorMap* ta = u.phase ? &p.tm_a_dn : &p.tm_a_up;
         const CUtensorMap* tb = u.phase ? &p.tm_b_dn : &p.tm_b_up;
         const int arow = tr * kTileM + static_cast<int>(rank) * kBM;
@@ -762,9 +799,8 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
     for (int idx = 0;; ++idx) {
       Unit u;
       if (!get_unit(p, cta, idx, u)) break;
-      const PhaseSched& s = u.phase ? p.dn : p.up;
       int tr, tq;
-      tile_coords(s, u.tile, tr, tq);
+      unit_coords(p, u, tr, tq);
       int ok = 1;
       if (lane == 0) ok = wait_bar(tfull_bar(acc), acc_phase, abort_flag, p, 400 + acc) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -790,10 +826,43 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       };
       float* ws_own = ws_row(cta);
 
+      // Fused reduce-scatter (down phase, tile finalised here): push to the owning rank, or
+      // (own band) wait for every other rank's partial of this tile.
+      bool rs_push = false, rs_reduce = false;
+      int rs_owner = 0;
+      size_t rs_tile = 0;
+      if constexpr (!SWAP && !PAIR) {
+        if (p.rs_world > 1 && u.phase == 1 && u.role != kRoleContrib) {
+          rs_owner = tr / p.rs_band_tiles;
+          rs_tile = static_cast<size_t>(tr - rs_owner * p.rs_band_tiles) * p.dn.tiles_q + tq;
+          rs_push = rs_owner != p.rs_rank;
+          rs_reduce = !rs_push;
+          if (rs_reduce) {
+            const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
+            if (lane == 0) {
+              for (int src = 0; src < p.rs_world && ok; ++src)
+                if (src != p.rs_rank)
+                  ok = wait_word_ge<true>(p.rs_flags[p.rs_rank] + src * band + rs_tile, 4u * p.epoch, abort_flag,
+                                          p, 4, src) ? 1 : 0;
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            for (int src = 0; src < p.rs_world; ++src)
+              if (src != p.rs_rank) (void)ld_acquire_sys(p.rs_flags[p.rs_rank] + src * band + rs_tile);
+          }
+        }
+      }
+      auto rs_slot = [&](int dst_rank, int src) {  // this thread's row of a staging slot
+        const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
+        const size_t slot = ((static_cast<size_t>(p.epoch & 1u) * p.rs_world + src) * band + rs_tile) * kBM + row;
+        return p.rs_stage[dst_rank] + slot * BN;
+      };
+
       if constexpr (!SWAP) {
         // Normal mode: tile rows are tokens, columns are features (H for up, N for down).
         const CUtensorMap* tms = u.phase ? &p.tm_st_y : &p.tm_st_hid;
-        const int orow = tr * kTileM + static_cast<int>(rank) * kBM + sub * 32;
+        const int orow = (rs_reduce ? (tr - p.rs_rank * p.rs_band_tiles) : tr) * kTileM +
+                         static_cast<int>(rank) * kBM + sub * 32;
 #pragma unroll 1
         for (int ch = 0; ch < BN / 64; ++ch) {
           float v[64];
@@ -820,9 +889,44 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
 #pragma unroll
             for (int j = 0; j < 64; ++j) v[j] = gelu<GELU>(v[j]);
           }
+          if (rs_reduce) {
+            // Ascending rank order: sum = p_0 + p_1 + ... (this rank's fp32 partial in place).
+            float acc[64];
+            bool first = true;
+#pragma unroll 1
+            for (int src = 0; src < p.rs_world; ++src) {
+              if (src == p.rs_rank) {
+#pragma unroll
+                for (int j = 0; j < 64; ++j) acc[j] = first ? v[j] : acc[j] + v[j];
+              } else {
+                const uint4* sp = reinterpret_cast<const uint4*>(rs_slot(p.rs_rank, src) + ch * 64);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const uint4 w = __ldcg(sp + j);
+                  const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float lo = unpack_lo<BF16>(wv[e]), hi = unpack_hi<BF16>(wv[e]);
+                    acc[8 * j + 2 * e] = first ? lo : acc[8 * j + 2 * e] + lo;
+                    acc[8 * j + 2 * e + 1] = first ? hi : acc[8 * j + 2 * e + 1] + hi;
+                  }
+                }
+              }
+              first = false;
+            }
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = acc[j];
+          }
           uint32_t pk[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) pk[j] = pack2<BF16>(v[2 * j], v[2 * j + 1]);
+          if (rs_push) {
+            // This thread's 64 columns of its row, straight into the owner's staging slot.
+            uint4* dp = reinterpret_cast<uint4*>(rs_slot(rs_owner, p.rs_rank) + ch * 64);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dp[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            continue;
+          }
           // Staging buffer (32 rows x 128 B, 128B-swizzled) owned by this warp.
           const uint32_t sb = sE + static_cast<uint32_t>((ew * 2 + sbuf) * kStageBufBytes);
           if (lane == 0) bulk_wait_read1();
@@ -887,6 +991,14 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       else mbar_arrive(tempty_bar(acc));
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
 
+      if (rs_push) {
+        // Publish this warp's 32 rows to the owning GPU: system-scope fence, then one
+        // release per warp on the owner's count for (this rank, tile).
+        __threadfence_system();
+        __syncwarp();
+        const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
+        if (lane == 0) red_release_sys_add(p.rs_flags[rs_owner] + p.rs_rank * band + rs_tile, 1u);
+      }
       if (u.role == kRoleContrib) {
         // Publish this warp's 32 rows of the partial: one release per warp, so the owner
         // waits for 4 signals per launch and no CTA-wide barrier is involved.

@@ -8,6 +8,9 @@ multi-GPU variants of the hot path):
   Y over all M rows; the partials are summed by an NCCL reduce-scatter over M (each rank
   keeps M/P rows of Y) or an all-reduce (every rank keeps Y).  M is processed in chunks so
   the collective of chunk i overlaps the kernel of chunk i+1 on NVLink.
+* **H-sharded with the reduce-scatter fused into the kernel**
+  (:class:`FusedTensorParallelFFN`): no NCCL call; the kernel's down-phase epilogue pushes
+  partial tiles to their owning GPU over NVLink and owners reduce them.
 * **M-sharded** (:class:`RowShardedFFN`): rank r holds rows ``[r*M/P, (r+1)*M/P)`` of X and
   full weights; no communication.
 
@@ -17,6 +20,7 @@ plain functions so they can be tested with CPU ``gloo`` ranks.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 
@@ -190,3 +194,108 @@ class RowShardedFFN:
 
     def check(self):
         self.prepared.check()
+
+
+def band_order(world: int, rank: int):
+    """Order in which ``rank`` visits the down phase's row bands under the fused
+    reduce-scatter: the other ranks' bands first (starting with the next rank), its own last."""
+    return [(rank + 1 + i) % world for i in range(world)]
+
+
+class FusedTensorParallelFFN:
+    """H-sharded fused FFN whose reduce-scatter runs inside the kernel, over NVLink.
+
+    Same partitioning as :class:`TensorParallelFFN` (rank r holds W1 rows / W2 columns of
+    ``h_slice(H, r, P)``), but no NCCL call: during the down phase each rank pushes the bf16
+    partial of every tile outside its own M/P-row band straight into the owning rank's
+    staging buffer (peer stores, then a system-scope release), and each rank sums the P
+    partials of its own band in ascending rank order and stores its Y rows.  Staging and
+    push-count buffers are CUDA IPC buffers exchanged once at construction.  :meth:`run`
+    launches one kernel and returns this rank's rows ``local_rows()`` of Y.
+    """
+
+    def __init__(self, x, w1, w2, *, group=None, sliced=False, down_impl="basic", block_num=None,
+                 gelu="rational", tile="cta128x256"):
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+        from .api import prepare_ffn
+        from .host.inputs import pitch_of
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        k = x.shape[-1]
+        m = x.numel() // k
+        if not sliced:
+            lo, hi = h_slice(w1.shape[0], self.rank, self.world)
+            w1, w2 = w1[lo:hi], w2[:, lo:hi]
+        w1, w2 = w1.contiguous(), w2.contiguous()
+        self.m, self.n = m, w2.shape[0]
+        self.prepared = prepare_ffn(x.reshape(m, k), w1, w2, down_impl=down_impl, block_num=block_num, gelu=gelu,
+                                    tile=tile)
+        lib = _lib.load()
+        h = self.prepared.handle
+        sb, fb = ctypes.c_uint64(), ctypes.c_uint64()
+        if lib.ffn_b200_reduce_scatter_bytes(h, self.world, ctypes.byref(sb), ctypes.byref(fb)) != _lib.OK:
+            raise ValueError("fused reduce-scatter needs M divisible by world*tile rows and a one-CTA prefill tile")
+        self._own = []
+        handles = []
+        with torch.cuda.device(x.device):
+            for size in (sb.value, fb.value):
+                ptr, ipc = ctypes.c_void_p(), (ctypes.c_char * 64)()
+                rc = lib.ffn_b200_peer_alloc(size, ctypes.byref(ptr), ipc)
+                if rc != _lib.OK:
+                    raise RuntimeError(f"ffn_b200_peer_alloc: {_lib.strerror(rc)}")
+                self._own.append(ptr)
+                handles.append(bytes(ipc))
+            everyone = [None] * self.world
+            dist.all_gather_object(everyone, handles, group=group)
+            self._opened = []
+            stage = (ctypes.c_void_p * self.world)()
+            flags = (ctypes.c_void_p * self.world)()
+            for r in range(self.world):
+                if r == self.rank:
+                    stage[r], flags[r] = self._own[0], self._own[1]
+                    continue
+                ptrs = []
+                for blob in everyone[r]:
+                    ptr = ctypes.c_void_p()
+                    rc = lib.ffn_b200_peer_open((ctypes.c_char * 64).from_buffer_copy(blob), ctypes.byref(ptr))
+                    if rc != _lib.OK:
+                        raise RuntimeError(f"ffn_b200_peer_open: {_lib.strerror(rc)}")
+                    self._opened.append(ptr)
+                    ptrs.append(ptr)
+                stage[r], flags[r] = ptrs
+            self.y = torch.empty((m // self.world, pitch_of(self.n)), dtype=x.dtype, device=x.device)
+            rc = lib.ffn_b200_set_reduce_scatter(h, self.world, self.rank, stage, flags, self.y.data_ptr(),
+                                                 self.y.stride(0))
+            if rc != _lib.OK:
+                raise ValueError(f"ffn_b200_set_reduce_scatter: {_lib.strerror(rc)}")
+            torch.cuda.synchronize()
+        dist.barrier(group=group)  # every rank has mapped every buffer before anyone pushes
+
+    def launches_per_run(self):
+        return 1
+
+    def run(self):
+        self.prepared.run()
+        return self.y[:, :self.n]
+
+    def local_rows(self):
+        per = self.m // self.world
+        return list(range(self.rank * per, (self.rank + 1) * per))
+
+    def check(self):
+        self.prepared.check()
+
+    def close(self):
+        from . import _lib
+
+        lib = _lib.load()
+        for ptr in getattr(self, "_opened", []):
+            lib.ffn_b200_peer_close(ptr)
+        for ptr in getattr(self, "_own", []):
+            lib.ffn_b200_peer_free(ptr)
+        self._opened, self._own = [], []

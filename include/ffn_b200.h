@@ -70,7 +70,8 @@ typedef enum {
   FFN_B200_KERNEL_OK = 0,
   FFN_B200_KERNEL_PIPE_TIMEOUT = 1, /* an on-chip pipeline wait ran past the wait limit */
   FFN_B200_KERNEL_DEP_TIMEOUT = 2,  /* a down tile waited too long for its hidden rows */
-  FFN_B200_KERNEL_SK_TIMEOUT = 3    /* a Stream-K owner waited too long for a partial */
+  FFN_B200_KERNEL_SK_TIMEOUT = 3,   /* a Stream-K owner waited too long for a partial */
+  FFN_B200_KERNEL_PEER_TIMEOUT = 4  /* a band owner waited too long for another GPU's partial */
 } ffn_b200_kernel_error;
 
 typedef struct {
@@ -166,6 +167,32 @@ FFN_B200_EXPORT int ffn_b200_set_wait_limit(ffn_b200_handle* handle, uint64_t na
 /* Test hook: 1 makes every down tile wait for one readiness signal too many, so the
  * bounded wait runs out and the kernel reports FFN_B200_KERNEL_DEP_TIMEOUT. */
 FFN_B200_EXPORT int ffn_b200_set_fault_injection(ffn_b200_handle* handle, int mode);
+
+/* ---- Multi-GPU (tensor parallel over H) with the reduce-scatter fused into the kernel ----
+ * Peer-visible device buffers: ffn_b200_peer_alloc allocates `bytes` (zeroed) on the current
+ * device and returns a 64-byte CUDA IPC handle; another process opens it with
+ * ffn_b200_peer_open (NVLink peer access), closes with ffn_b200_peer_close; the owner frees
+ * with ffn_b200_peer_free.  Reference counterpart: none (the reference is single-device;
+ * this replaces an NCCL reduce-scatter after the kernel). */
+FFN_B200_EXPORT int ffn_b200_peer_alloc(uint64_t bytes, void** dev_ptr, void* ipc_handle);
+FFN_B200_EXPORT int ffn_b200_peer_open(const void* ipc_handle, void** dev_ptr);
+FFN_B200_EXPORT int ffn_b200_peer_close(void* dev_ptr);
+FFN_B200_EXPORT int ffn_b200_peer_free(void* dev_ptr);
+
+/* Sizes of one rank's staging buffer (bf16 partial tiles, two launch parities) and push
+ * counts for a `world`-GPU reduce-scatter of this handle's down phase. */
+FFN_B200_EXPORT int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* handle, int world, uint64_t* stage_bytes,
+                                                  uint64_t* flag_bytes);
+
+/* Turns the handle's down phase into a fused reduce-scatter over `world` GPUs: this rank
+ * (`rank`) owns Y rows [rank*M/world, (rank+1)*M/world), written to `y_local`
+ * ([M/world, ldy_local]); stage_ptrs[r] / flag_ptrs[r] are rank r's staging and count
+ * buffers as mapped in this process (own ones included).  Every rank runs its handle once
+ * per step; partial tiles of other bands are pushed over NVLink during the epilogue and
+ * summed by their owner in ascending rank order.  Needs M divisible by world*128 and a
+ * one-CTA prefill tile.  After a kernel error all ranks reset together. */
+FFN_B200_EXPORT int ffn_b200_set_reduce_scatter(ffn_b200_handle* handle, int world, int rank, void* const* stage_ptrs,
+                                                void* const* flag_ptrs, void* y_local, int64_t ldy_local);
 
 /* Tracing: when `device_stamps` (a device uint64[block_num][8], or NULL to switch off) is
  * set, every later run writes per-CTA %globaltimer stamps (ns): 0 setup done, 1 first TMA

@@ -14,7 +14,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from ffn_optim_b200.sharded import chunk_rows, combine_partials, h_slice, m_slices, scattered_rows
+from ffn_optim_b200.sharded import band_order, chunk_rows, combine_partials, h_slice, m_slices, scattered_rows
 from oracle import ffn_oracle as O
 
 
@@ -40,6 +40,17 @@ def test_m_slices_and_chunks():
         chunk_rows(6993, 2, 4)
     rows = sorted(r for rank in range(8) for r in scattered_rows(ch, rank, 8))
     assert rows == list(range(65536))
+
+
+def test_band_order_puts_own_band_last():
+    for world in (2, 3, 8):
+        for rank in range(world):
+            order = band_order(world, rank)
+            assert sorted(order) == list(range(world)) and order[-1] == rank
+            # every other rank's band comes before this rank's own band
+            for other in range(world):
+                if other != rank:
+                    assert band_order(world, other).index(rank) < world - 1
 
 
 def _free_port():
