@@ -42,7 +42,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="cfg5_bf16")
-    ap.add_argument("--shard", choices=("h", "hf", "m"), default="h",
+    ap.add_argument("--shard", choices=("h", "hf", "m"), default="m",
                     help="N>1: h = H-sharded + NCCL reduce-scatter, hf = H-sharded with the reduce-scatter "
                          "fused into the kernel (NVLink peer stores), m = M-sharded")
     ap.add_argument("--chunks", type=int, default=4)

@@ -589,9 +589,14 @@ int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, void* c
   P.rs_world = world;
   P.rs_rank = rank;
   P.rs_band_tiles = pl.down.tiles_r / world;
+  const int64_t stage_rows = 2ll * world * (pl.down.tiles_r / world) * pl.down.tiles_q * ffnb200::kBM;
   for (int r = 0; r < world; ++r) {
     P.rs_stage[r] = static_cast<uint16_t*>(stage_ptrs[r]);
     P.rs_flags[r] = static_cast<unsigned*>(flag_ptrs[r]);
+    // Bulk-store map over rank r's staging buffer ([rows][tile_n], no multicast).
+    const int e = encode_2d(&P.tm_rs[r], stage_ptrs[r], h->prob.dtype, pl.tile_n, stage_rows, pl.tile_n, 64,
+                            ffnb200::kStoreRows);
+    if (e) return e;
   }
   return FFN_B200_OK;
 }

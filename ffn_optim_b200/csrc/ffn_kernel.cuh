@@ -87,7 +87,10 @@ struct Params {
   int rs_world, rs_rank, rs_band_tiles;
   uint16_t* rs_stage[kMaxRanks];   // per rank: [2 parity][world][band tiles][kBM][BN] bf16
   unsigned* rs_flags[kMaxRanks];   // per rank: [world][band tiles] push counts (4 per launch)
+  CUtensorMap tm_rs[kMaxRanks];    // store maps over each rank's staging, viewed as [rows][BN]
 };
+
+static_assert(sizeof(Params) <= 4096, "kernel parameters must fit the 4 KB parameter space");
 
 // Per-CTA trace stamps (ns, %globaltimer) written when Params::trace is set.
 enum TraceSlot : int {
@@ -920,13 +923,6 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
           uint32_t pk[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) pk[j] = pack2<BF16>(v[2 * j], v[2 * j + 1]);
-          if (rs_push) {
-            // This thread's 64 columns of its row, straight into the owner's staging slot.
-            uint4* dp = reinterpret_cast<uint4*>(rs_slot(rs_owner, p.rs_rank) + ch * 64);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) dp[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-            continue;
-          }
           // Staging buffer (32 rows x 128 B, 128B-swizzled) owned by this warp.
           const uint32_t sb = sE + static_cast<uint32_t>((ew * 2 + sbuf) * kStageBufBytes);
           if (lane == 0) bulk_wait_read1();
@@ -941,7 +937,16 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
           fence_async_shared();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(tms, sb, tq * BN + ch * 64, orow);
+            if (rs_push) {
+              // The owner's staging slot (this rank's partial of the tile): one 4 KB bulk
+              // store over NVLink per chunk and warp.
+              const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
+              const int srow = static_cast<int>(((static_cast<size_t>(p.epoch & 1u) * p.rs_world + p.rs_rank) * band +
+                                                 rs_tile) * kBM) + sub * 32;
+              tma_store_2d(&p.tm_rs[rs_owner], sb, ch * 64, srow);
+            } else {
+              tma_store_2d(tms, sb, tq * BN + ch * 64, orow);
+            }
             bulk_commit();
           }
           sbuf ^= 1;
@@ -992,12 +997,16 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
 
       if (rs_push) {
-        // Publish this warp's 32 rows to the owning GPU: system-scope fence, then one
-        // release per warp on the owner's count for (this rank, tile).
-        __threadfence_system();
-        __syncwarp();
+        // Publish this warp's 32 rows to the owning GPU: the bulk stores complete, the async
+        // proxy is ordered before the generic one, then one system-scope release per warp on
+        // the owner's count for (this rank, tile).
         const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
-        if (lane == 0) red_release_sys_add(p.rs_flags[rs_owner] + p.rs_rank * band + rs_tile, 1u);
+        if (lane == 0) {
+          bulk_wait_all();
+          fence_async_global();
+          red_release_sys_add(p.rs_flags[rs_owner] + p.rs_rank * band + rs_tile, 1u);
+        }
+        __syncwarp();
       }
       if (u.role == kRoleContrib) {
         // Publish this warp's 32 rows of the partial: one release per warp, so the owner

@@ -102,7 +102,7 @@ class TensorParallelFFN:
     """
 
     def __init__(self, x, w1, w2, *, group=None, mode="reduce_scatter", chunks=4, sliced=False,
-                 down_impl="basic", block_num=None, gelu="rational", tile=None):
+                 down_impl="basic", block_num=None, gelu="rational", tile=None, reserve_sms=16):
         import torch
         import torch.distributed as dist
 
@@ -126,6 +126,11 @@ class TensorParallelFFN:
         self.n = w2.shape[0]
         self.m = m
         x2 = x.reshape(m, k)
+        # The fused kernel is persistent (one CTA per SM); leaving `reserve_sms` SMs free lets
+        # NCCL's collective kernels run beside it, so chunk i's reduce-scatter overlaps the
+        # kernel of chunk i+1 instead of waiting for it.
+        if block_num is None and reserve_sms:
+            block_num = torch.cuda.get_device_properties(x.device).multi_processor_count - int(reserve_sms)
         rows = chunk_rows(m, self.world, chunks) if mode == "reduce_scatter" else [(0, m)]
         self.chunks = []
         for lo, hi in rows:
