@@ -80,31 +80,49 @@ def traffic_for(workload):
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons around the timed region.
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    Sampling starts before the timed region (nvidia-smi needs a moment to produce its first
+    line); every sample carries nvidia-smi's timestamp and only samples inside
+    [begin, end] of the timed region count -- or, when the region is shorter than the
+    sampling period, the samples closest to it."""
+
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.lines = []
         self.thread = None
+        self.window = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0:
+                time.sleep(0.02)
         except OSError:
             self.proc = None
 
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def begin(self):
+        self.window = [time.time(), None]
+
+    def end(self):
+        if self.window:
+            self.window[1] = time.time()
+        time.sleep(0.12)  # let the sample after the region arrive
 
     def stop(self):
         if self.proc is None:
@@ -115,23 +133,29 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.thread.join(timeout=2)
-        sm, smax, reasons, power = [], None, set(), []
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        from datetime import datetime
+
+        samples = []
         for line in self.lines:
-            parts = [s.strip() for s in line.split(",")]
-            if len(parts) < 8:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[0]))
-                smax = float(parts[1])
-                power.append(float(parts[2]))
+                ts = time.mktime(datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timetuple()) + \
+                    datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").microsecond / 1e6
+                samples.append((ts, float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[4:8]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm), "power_w_max": max(power) if power else None}
+        inside = samples
+        if self.window and self.window[1] and samples:
+            b, e = self.window
+            inside = [x for x in samples if b - 0.05 <= x[0] <= e + 0.05]
+            if not inside:  # region shorter than the sampling period: the nearest samples
+                inside = sorted(samples, key=lambda x: min(abs(x[0] - b), abs(x[0] - e)))[:2]
+        sm = [x[1] for x in inside]
+        reasons = sorted({name for x in inside for name, val in zip(self.REASONS, x[4]) if val.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": inside[0][2] if inside else None,
+                "reasons": reasons, "samples": len(inside), "power_w_max": max(x[3] for x in inside) if inside else None}
 
 
 def device_inputs(case, device, seed=7):
@@ -292,6 +316,10 @@ def main():
     scrub = torch.empty(4 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
     sampler = ClockSampler(local)
     sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.begin()
     if flush:
         # Each step timed alone; an L2-sized write between steps evicts the operands.
         ms = 0.0
@@ -313,6 +341,7 @@ def main():
         end.record()
         end.synchronize()
         ms = start.elapsed_time(end)
+    sampler.end()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
