@@ -52,7 +52,8 @@ class Problem(ctypes.Structure):
 
 class PhasePlan(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in
-                ("tiles_r", "tiles_q", "tiles", "k_blocks", "dp_tiles", "sk_tiles", "sk_iters", "sk_rem", "group")]
+                ("tiles_r", "tiles_q", "tiles", "k_blocks", "dp_tiles", "sk_tiles", "sk_iters", "sk_rem", "group",
+                 "sk_ctas")]
 
     def to_dict(self):
         return {name: getattr(self, name) for name, _ in self._fields_}

@@ -30,52 +30,60 @@ struct Variant {
   int bn, stages;
   bool swap, pair;
   int ksub;  // 64-wide K sub-blocks per pipeline stage
+  int epi;   // epilogue warps (4, or 8 = two per TMEM sub-partition for short tiles)
 };
 // 0: prefill tiles 128x256 (one CTA), 1: 128x128 for small grids, 2/3: swap-AB decode
 // tiles (16 / 64 tokens), 4: prefill tiles 256x256 computed by a CTA pair (cta_group::2),
-// 5/6: swap-AB decode tiles with 256-wide K stages (longer contiguous weight reads).
-constexpr Variant kVariants[] = {{256, 4, false, false, 1}, {128, 6, false, false, 1}, {16, 8, true, false, 1},
-                                 {64, 8, true, false, 1},   {256, 6, false, true, 1},  {16, 3, true, false, 4},
-                                 {64, 4, true, false, 2}};
+// 5/6: swap-AB decode tiles with 256/128-wide K stages (longer contiguous weight reads).
+constexpr Variant kVariants[] = {{256, 4, false, false, 1, 4}, {128, 4, false, false, 1, 8},
+                                 {16, 8, true, false, 1, 8},   {64, 8, true, false, 1, 8},
+                                 {256, 6, false, true, 1, 4},  {16, 3, true, false, 4, 8},
+                                 {64, 4, true, false, 2, 8}};
 constexpr int kNumVariants = 7;
 
-template <int BN, int ST, bool SW, bool PR, int KS>
+template <int BN, int ST, bool SW, bool PR, int KS, int EP>
 KernelFn pick_kernel(int bf16, int gelu) {
   using namespace ffnb200;
   if (bf16)
-    return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, true, 1> : ffn_fused_kernel<BN, ST, SW, PR, KS, true, 0>;
-  return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, false, 1> : ffn_fused_kernel<BN, ST, SW, PR, KS, false, 0>;
+    return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, EP, true, 1> : ffn_fused_kernel<BN, ST, SW, PR, KS, EP, true, 0>;
+  return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, EP, false, 1> : ffn_fused_kernel<BN, ST, SW, PR, KS, EP, false, 0>;
 }
+#define FFN_B200_VARIANTS(X)                  \
+  X(0, 256, 4, false, false, 1, 4)            \
+  X(1, 128, 4, false, false, 1, 8)            \
+  X(2, 16, 8, true, false, 1, 8)              \
+  X(3, 64, 8, true, false, 1, 8)              \
+  X(4, 256, 6, false, true, 1, 4)             \
+  X(5, 16, 3, true, false, 4, 8)              \
+  X(6, 64, 4, true, false, 2, 8)
 KernelFn kernel_for(int variant, int bf16, int gelu) {
   switch (variant) {
-    case 0: return pick_kernel<256, 4, false, false, 1>(bf16, gelu);
-    case 1: return pick_kernel<128, 6, false, false, 1>(bf16, gelu);
-    case 2: return pick_kernel<16, 8, true, false, 1>(bf16, gelu);
-    case 3: return pick_kernel<64, 8, true, false, 1>(bf16, gelu);
-    case 4: return pick_kernel<256, 6, false, true, 1>(bf16, gelu);
-    case 5: return pick_kernel<16, 3, true, false, 4>(bf16, gelu);
-    case 6: return pick_kernel<64, 4, true, false, 2>(bf16, gelu);
+#define X(id, bn, st, sw, pr, ks, ep) \
+  case id: return pick_kernel<bn, st, sw, pr, ks, ep>(bf16, gelu);
+    FFN_B200_VARIANTS(X)
+#undef X
   }
   return nullptr;
 }
 int smem_for(int variant) {
   switch (variant) {
-    case 0: return ffnb200::Layout<256, 4, false, false, 1>::kSmem;
-    case 1: return ffnb200::Layout<128, 6, false, false, 1>::kSmem;
-    case 2: return ffnb200::Layout<16, 8, true, false, 1>::kSmem;
-    case 3: return ffnb200::Layout<64, 8, true, false, 1>::kSmem;
-    case 4: return ffnb200::Layout<256, 6, false, true, 1>::kSmem;
-    case 5: return ffnb200::Layout<16, 3, true, false, 4>::kSmem;
-    case 6: return ffnb200::Layout<64, 4, true, false, 2>::kSmem;
+#define X(id, bn, st, sw, pr, ks, ep) \
+  case id: return ffnb200::Layout<bn, st, sw, pr, ks, ep>::kSmem;
+    FFN_B200_VARIANTS(X)
+#undef X
   }
   return 0;
 }
+int threads_for(int variant) { return ffnb200::kCtrlThreads + 32 * kVariants[variant].epi; }
 int tmem_cols_for(int variant) {
   const int c = 2 * kVariants[variant].bn;
   return c < 32 ? 32 : c;
 }
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+constexpr int kMinSplitKBlocks = 32;  // see make_plan: the up phase splits only tiles this long
+constexpr int kMinSegment = 8;        // minimum K steps of one CTA's Stream-K share
 
 struct PhaseInput {
   int64_t rows, cols, depth;
@@ -99,13 +107,19 @@ int phase_plan(const PhaseInput& in, int tile_m, int bn, int tile_k, int C, bool
   if (split) {
     const int64_t sk = T % C;
     const int64_t iters = sk * L;
+    // Each share gets at least kMinSegment K steps: short tails go to fewer CTAs, so an
+    // owner never waits for, and reads, more partials than the split saves.
+    int64_t ctas = iters / kMinSegment;
+    ctas = ctas < 1 ? 1 : (ctas > C ? C : ctas);
     out->sk_tiles = static_cast<int32_t>(sk);
     out->dp_tiles = static_cast<int32_t>(T - sk);
-    out->sk_iters = static_cast<int32_t>(iters / C);
-    out->sk_rem = static_cast<int32_t>(iters % C);
+    out->sk_ctas = static_cast<int32_t>(ctas);
+    out->sk_iters = static_cast<int32_t>(iters / ctas);
+    out->sk_rem = static_cast<int32_t>(iters % ctas);
   } else {
     out->sk_tiles = 0;
     out->dp_tiles = static_cast<int32_t>(T);
+    out->sk_ctas = 0;
     out->sk_iters = 0;
     out->sk_rem = 0;
   }
@@ -257,8 +271,11 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   const int tile_k = ffnb200::kBK * v.ksub;
   int rc = phase_plan(up, tile_m, v.bn, tile_k, C, false, group, &probe);
   if (rc) return rc;
+  // Splitting only pays when a tile's mainloop outlasts the partial exchange and fixup
+  // (measured ~5-10 us): short tiles (fewer than kMinSplitKBlocks stages) stay whole even
+  // if the last wave leaves SMs idle.
   const int64_t waves = cdiv(probe.tiles, C);
-  const bool up_split = (probe.tiles % C) != 0 && probe.k_blocks >= 2 &&
+  const bool up_split = (probe.tiles % C) != 0 && probe.k_blocks >= kMinSplitKBlocks &&
                         static_cast<double>(probe.tiles) < 0.9 * static_cast<double>(waves * C);
   rc = phase_plan(up, tile_m, v.bn, tile_k, C, up_split, group, &out->up);
   if (rc) return rc;
@@ -365,6 +382,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     PhaseSched s;
     s.tiles_r = pp.tiles_r; s.tiles_q = pp.tiles_q; s.T = pp.tiles; s.L = pp.k_blocks;
     s.dp = pp.dp_tiles; s.sk = pp.sk_tiles; s.q = pp.sk_iters; s.rem = pp.sk_rem; s.group = pp.group;
+    s.skc = pp.sk_ctas;
     return s;
   };
   P.up = to_sched(plan.up);
@@ -377,8 +395,8 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
   P.l2_hints = prob.l2_policy == 2 ? 1 : 0;
-  // Readiness counters gain 4 * ncta * (up tiles per row block) per launch, flags 4 per launch.
-  const int64_t per_blk = 4ll * ncta * (sw ? plan.up.tiles_r : plan.up.tiles_q);
+  // Readiness counters gain epi * ncta * (up tiles per row block) per launch, flags epi per launch.
+  const int64_t per_blk = static_cast<int64_t>(kVariants[plan.variant].epi) * ncta * (sw ? plan.up.tiles_r : plan.up.tiles_q);
   h->epoch_limit = static_cast<unsigned>(((int64_t(1) << 30) / (per_blk > 4 ? per_blk : 4)));
 
   int cur = 0;
@@ -393,7 +411,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(static_cast<unsigned>(plan.block_num), 1, 1);
-    cfg.blockDim = dim3(ffnb200::kThreads, 1, 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads_for(plan.variant)), 1, 1);
     cfg.dynamicSmemBytes = static_cast<size_t>(plan.smem_bytes);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -455,7 +473,7 @@ int ffn_b200_run(ffn_b200_handle* h, void* stream) {
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(static_cast<unsigned>(h->plan.block_num), 1, 1);
-  cfg.blockDim = dim3(ffnb200::kThreads, 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads_for(h->plan.variant)), 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(h->plan.smem_bytes);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -638,6 +656,7 @@ namespace ffnb200 {
 void (*internal_kernel_for(int variant, int bf16, int gelu))(const Params) {
   return kernel_for(variant, bf16, gelu);
 }
+int internal_threads_for(int variant) { return threads_for(variant); }
 int internal_encode_2d(CUtensorMap* tm, const void* base, int dtype, int64_t inner, int64_t outer, int64_t pitch,
                        uint32_t box_inner, uint32_t box_outer) {
   const int rc = get_encode();

@@ -43,8 +43,7 @@ namespace ffnb200 {
 
 constexpr int kBM = 128;          // MMA M (rows of the A operand per tile)
 constexpr int kBK = 64;           // K per pipeline stage = one 128-byte swizzle atom of 16-bit data
-constexpr int kThreads = 192;     // 6 warps
-constexpr int kEpiThreads = 128;  // warps 2..5
+constexpr int kCtrlThreads = 64;  // warp 0 (TMA producer) + warp 1 (MMA issuer); epilogue warps follow
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kStoreRows = 32;    // rows per epilogue warp (one TMEM sub-partition)
 constexpr int kStageBufBytes = kStoreRows * 128;  // 32 rows x 64 x 16-bit, 128B-swizzled
@@ -56,6 +55,7 @@ struct PhaseSched {
   int tiles_r, tiles_q, T, L;  // tile grid, tiles, k-blocks per tile
   int dp, sk, q, rem;          // data-parallel tiles, Stream-K tiles, k-blocks per CTA (+1 if c < rem)
   int group;                   // raster group height in tile rows
+  int skc;                     // CTAs sharing the Stream-K tail (the first skc)
 };
 
 struct Params {
@@ -333,6 +333,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Shared-memory matrix descriptor: K-major tile of 128-byte rows, 128B swizzle, 8-row
 // swizzle atoms 1024 B apart (SBO), descriptor version 1 (sm_100).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -456,7 +468,7 @@ __device__ __forceinline__ bool get_unit(const Params& p, int c, int idx, Unit& 
     }
     idx -= n_dp;
     int n_sk = 0, st = 0, en = 0;
-    if (s.sk > 0) {
+    if (s.sk > 0 && c < s.skc) {
       st = sk_start(s, c);
       en = sk_start(s, c + 1);
       if (en > st) n_sk = (en - 1) / s.L - st / s.L + 1;
@@ -535,21 +547,24 @@ __device__ __forceinline__ bool wait_word_ge(const unsigned* word, unsigned targ
 // ------------------------------------------------------------------------------------------
 // The kernel
 // ------------------------------------------------------------------------------------------
-template <int BN, int STAGES, bool SWAP, bool PAIR = false, int KSUB = 1>
+template <int BN, int STAGES, bool SWAP, bool PAIR = false, int KSUB = 1, int EPI = 4>
 struct Layout {
+  static constexpr int kEpiWarps = EPI;             // 4, or 8 = two warps per TMEM sub-partition
+  static constexpr int kThreads = kCtrlThreads + 32 * EPI;
   static constexpr int kNcta = PAIR ? 2 : 1;       // CTAs per tile (cluster size)
   static constexpr int kBRows = BN / kNcta;         // B rows each CTA loads per stage
   static constexpr int kBSub = kBRows * kBK * 2;    // one 64-wide K sub-block of B
   static constexpr int kAStage = KSUB * kABytes;    // a stage holds KSUB adjacent K sub-blocks
   static constexpr int kBStage = KSUB * kBSub;
   static constexpr int kStageBytes = kAStage + kBStage;
-  static constexpr int kEpiBytes = SWAP ? 0 : 4 * 2 * kStageBufBytes;
+  static constexpr int kEpiBytes = SWAP ? 0 : EPI * 2 * kStageBufBytes;
   static constexpr int kBarBytes = 256;
   static constexpr int kSmem = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiBytes + kBarBytes;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static_assert((kBSub % 1024) == 0, "B tile must be whole swizzle atoms");
   static_assert((2 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");
   static_assert(!PAIR || !SWAP, "CTA pairs are used for prefill tiles only");
+  static_assert(EPI == 4 || EPI == 8, "epilogue warps: one or two per TMEM sub-partition");
 };
 
 // PAIR = true: a cluster of two CTAs computes one 256 x BN tile with tcgen05 cta_group::2.
@@ -558,9 +573,14 @@ struct Layout {
 // barrier; the leader's MMA thread issues the pair MMAs, whose D lands 128 rows in each
 // CTA's TMEM, and its tcgen05.commit arrives on the empty / tmem-full barriers of both CTAs;
 // each CTA's epilogue stores its own 128 rows and releases the accumulator on the leader.
-template <int BN, int STAGES, bool SWAP, bool PAIR, int KSUB, bool BF16, int GELU>
-__global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_constant__ Params p) {
-  using LY = Layout<BN, STAGES, SWAP, PAIR, KSUB>;
+template <int BN, int STAGES, bool SWAP, bool PAIR, int KSUB, int EPI, bool BF16, int GELU>
+__global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(const __grid_constant__ Params p) {
+  using LY = Layout<BN, STAGES, SWAP, PAIR, KSUB, EPI>;
+  constexpr int kParts = EPI / 4;  // epilogue warps per TMEM sub-partition, each takes a column share
+  // Swap mode reads TMEM in chunks of kCW token columns; normal mode in 64-column chunks.
+  constexpr int kCW = SWAP ? (BN / kParts < 16 ? BN / kParts : 16) : 64;
+  constexpr int kChunks = BN / kCW;
+  static_assert(kChunks % kParts == 0, "column chunks split evenly over the warps of a sub-partition");
   constexpr int kNcta = LY::kNcta;
   constexpr int kTileM = kBM * kNcta;
   constexpr uint32_t kIdesc = make_idesc<BF16, BN, kTileM>();
@@ -598,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), kEpiThreads * kNcta);
+      mbar_init(tempty_bar(a), 32 * EPI * kNcta);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -632,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       uint32_t phase = 0;
       long long issued = 0;
       int ready_blk = -1;
-      const unsigned per_blk = 4u * kNcta * static_cast<unsigned>(SWAP ? p.up.tiles_r : p.up.tiles_q);
+      const unsigned per_blk = static_cast<unsigned>(EPI * kNcta) * static_cast<unsigned>(SWAP ? p.up.tiles_r : p.up.tiles_q);
       const unsigned target = p.epoch * per_blk + (p.inject ? 1u : 0u);
       // Optional L2 policy (off by default: on cfg5 it raised DRAM reads from 62 GB to 430 GB).
       const uint64_t pol_a = policy_evict_last();
@@ -793,7 +813,10 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     const int ew = warp - 2;            // staging-buffer owner index
     const int sub = warp & 3;           // TMEM lane sub-partition this warp may access
+    const int part = ew >> 2;           // which share of the columns this warp handles
     const int row = sub * 32 + lane;    // row inside this CTA's 128 rows of the tile
+    constexpr int kMyChunks = kChunks / kParts;
+    const int ch0 = part * kMyChunks;
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
@@ -815,7 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
       if (u.role == kRoleOwner && u.c_first <= u.c_last) {
         if (lane == 0) {
           for (int c2 = u.c_first; c2 <= u.c_last && ok; ++c2)
-            ok = wait_word_ge(p.flags + (u.phase * p.C + c2) * kNcta + slot_base, 4u * p.epoch, abort_flag, p, 3,
+            ok = wait_word_ge(p.flags + (u.phase * p.C + c2) * kNcta + slot_base, EPI * p.epoch, abort_flag, p, 3,
                               c2) ? 1 : 0;
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -845,7 +868,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
             if (lane == 0) {
               for (int src = 0; src < p.rs_world && ok; ++src)
                 if (src != p.rs_rank)
-                  ok = wait_word_ge<true>(p.rs_flags[p.rs_rank] + src * band + rs_tile, 4u * p.epoch, abort_flag,
+                  ok = wait_word_ge<true>(p.rs_flags[p.rs_rank] + src * band + rs_tile, EPI * p.epoch, abort_flag,
                                           p, 4, src) ? 1 : 0;
             }
             ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -867,7 +890,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
         const int orow = (rs_reduce ? (tr - p.rs_rank * p.rs_band_tiles) : tr) * kTileM +
                          static_cast<int>(rank) * kBM + sub * 32;
 #pragma unroll 1
-        for (int ch = 0; ch < BN / 64; ++ch) {
+        for (int ch = ch0; ch < ch0 + kMyChunks; ++ch) {
           float v[64];
           tmem_ld32(tbase + ch * 64, v);
           tmem_ld32(tbase + ch * 64 + 32, v + 32);
@@ -893,32 +916,34 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
             for (int j = 0; j < 64; ++j) v[j] = gelu<GELU>(v[j]);
           }
           if (rs_reduce) {
-            // Ascending rank order: sum = p_0 + p_1 + ... (this rank's fp32 partial in place).
-            float acc[64];
-            bool first = true;
+            // Ascending rank order: sum = p_0 + p_1 + ... (this rank's fp32 partial in place),
+            // 16 columns at a time to keep the register peak of the chunk loop.
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float acc[16];
 #pragma unroll 1
-            for (int src = 0; src < p.rs_world; ++src) {
-              if (src == p.rs_rank) {
+              for (int src = 0; src < p.rs_world; ++src) {
+                if (src == p.rs_rank) {
 #pragma unroll
-                for (int j = 0; j < 64; ++j) acc[j] = first ? v[j] : acc[j] + v[j];
-              } else {
-                const uint4* sp = reinterpret_cast<const uint4*>(rs_slot(p.rs_rank, src) + ch * 64);
+                  for (int j = 0; j < 16; ++j) acc[j] = src == 0 ? v[16 * q + j] : acc[j] + v[16 * q + j];
+                } else {
+                  const uint4* sp = reinterpret_cast<const uint4*>(rs_slot(p.rs_rank, src) + ch * 64 + 16 * q);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const uint4 w = __ldcg(sp + j);
-                  const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+                  for (int j = 0; j < 2; ++j) {
+                    const uint4 w = __ldcg(sp + j);
+                    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const float lo = unpack_lo<BF16>(wv[e]), hi = unpack_hi<BF16>(wv[e]);
-                    acc[8 * j + 2 * e] = first ? lo : acc[8 * j + 2 * e] + lo;
-                    acc[8 * j + 2 * e + 1] = first ? hi : acc[8 * j + 2 * e + 1] + hi;
+                    for (int e = 0; e < 4; ++e) {
+                      const float lo = unpack_lo<BF16>(wv[e]), hi = unpack_hi<BF16>(wv[e]);
+                      acc[8 * j + 2 * e] = src == 0 ? lo : acc[8 * j + 2 * e] + lo;
+                      acc[8 * j + 2 * e + 1] = src == 0 ? hi : acc[8 * j + 2 * e + 1] + hi;
+                    }
                   }
                 }
               }
-              first = false;
-            }
 #pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] = acc[j];
+              for (int j = 0; j < 16; ++j) v[16 * q + j] = acc[j];
+            }
           }
           uint32_t pk[32];
 #pragma unroll
@@ -958,21 +983,22 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
         uint16_t* out = reinterpret_cast<uint16_t*>(u.phase ? p.y : p.hidden);
         const long long ld = u.phase ? p.ldy : p.ldh;
 #pragma unroll 1
-        for (int ch = 0; ch < BN / 16; ++ch) {
-          float v[16];
-          tmem_ld16(tbase + ch * 16, v);
+        for (int ch = ch0; ch < ch0 + kMyChunks; ++ch) {
+          float v[kCW];
+          if constexpr (kCW == 16) tmem_ld16(tbase + ch * kCW, v);
+          else tmem_ld8(tbase + ch * kCW, v);
           if (u.role == kRoleContrib) {
-            float4* dst = reinterpret_cast<float4*>(ws_own + ch * 16);
+            float4* dst = reinterpret_cast<float4*>(ws_own + ch * kCW);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int j = 0; j < kCW / 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             continue;
           }
           if (u.role == kRoleOwner) {
 #pragma unroll 1
             for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
-              const float4* src = reinterpret_cast<const float4*>(ws_row(c2) + ch * 16);
+              const float4* src = reinterpret_cast<const float4*>(ws_row(c2) + ch * kCW);
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
+              for (int j = 0; j < kCW / 4; ++j) {
                 const float4 t = __ldcg(src + j);
                 v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
               }
@@ -980,8 +1006,8 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fused_kernel(const __grid_con
           }
           if (feat < F) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = tq * BN + ch * 16 + j;
+            for (int j = 0; j < kCW; ++j) {
+              const int m = tq * BN + ch * kCW + j;
               if (m < p.M) {
                 const float val = u.phase == 0 ? gelu<GELU>(v[j]) : v[j];
                 out[static_cast<long long>(m) * ld + feat] = cvt1<BF16>(val);

@@ -33,6 +33,7 @@ namespace ffnb200 {
 void (*internal_kernel_for(int variant, int bf16, int gelu))(const Params);
 int internal_encode_2d(CUtensorMap* tm, const void* base, int dtype, int64_t inner, int64_t outer, int64_t pitch,
                        uint32_t box_inner, uint32_t box_outer);
+int internal_threads_for(int variant);
 }  // namespace ffnb200
 
 // The scratch.  In host code this name is only a stand-in for the symbol; the device address
@@ -139,6 +140,7 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
     PhaseSched s;
     s.tiles_r = pp.tiles_r; s.tiles_q = pp.tiles_q; s.T = pp.tiles; s.L = pp.k_blocks;
     s.dp = pp.dp_tiles; s.sk = pp.sk_tiles; s.q = pp.sk_iters; s.rem = pp.sk_rem; s.group = pp.group;
+    s.skc = pp.sk_ctas;
     return s;
   };
   P.hidden = hidden;
@@ -177,7 +179,7 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(static_cast<unsigned>(plan.block_num), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(internal_threads_for(plan.variant)), 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(plan.smem_bytes);
   cfg.stream = sh;
   cudaLaunchAttribute attr[1];

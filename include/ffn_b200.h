@@ -93,12 +93,13 @@ typedef struct {
 /* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
  * rows/cols are the tile grid of the MMA's A and B operands; k_blocks is the number of
  * tile_k-wide K steps (pipeline stages) per tile.  dp_tiles are computed whole by one CTA; the sk_tiles tail
- * is split along K over all CTAs (Stream-K), sk_iters (+1 for the first sk_rem CTAs)
- * K steps per CTA. */
+ * is split along K over the first sk_ctas CTAs (Stream-K), sk_iters (+1 for the first
+ * sk_rem CTAs) K steps per CTA. */
 typedef struct {
   int32_t tiles_r, tiles_q, tiles, k_blocks;
   int32_t dp_tiles, sk_tiles, sk_iters, sk_rem;
   int32_t group;
+  int32_t sk_ctas; /* CTAs sharing the Stream-K tail (the first sk_ctas; each gets >= 8 K steps) */
 } ffn_b200_phase_plan;
 
 typedef struct {

@@ -114,7 +114,7 @@ def _units(phase, C):
     for c in range(C):
         for t in range(c, phase["dp_tiles"], C):
             units.append((c, t, 0, phase["k_blocks"], "full"))
-        if phase["sk_tiles"]:
+        if phase["sk_tiles"] and c < phase["sk_ctas"]:
             q, r, L = phase["sk_iters"], phase["sk_rem"], phase["k_blocks"]
             st, en = c * q + min(c, r), (c + 1) * q + min(c + 1, r)
             i = st
@@ -160,6 +160,8 @@ def test_plan_covers_every_k_block_once(case_id, tile):
                     owners[t] = owners.get(t, 0) + 1
             assert len(cover) == ph["tiles"] * ph["k_blocks"] and set(cover.values()) == {1}
             assert len(owners) == ph["tiles"] and set(owners.values()) == {1}
+            if ph["sk_tiles"]:
+                assert 1 <= ph["sk_ctas"] <= owners_n and ph["sk_iters"] >= 8 or ph["sk_ctas"] == 1
         if down == "basic":
             assert k["down"]["sk_tiles"] == 0
 
