@@ -37,7 +37,7 @@ def _worker(rank, world, port, out_dir):
     from ffn_optim_b200 import prepare_ffn
     from ffn_optim_b200.sharded import FusedTensorParallelFFN, RowShardedFFN, TensorParallelFFN
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
@@ -78,3 +78,52 @@ def test_sharded_variants_match_single_gpu(tmp_path):
         _close("nccl", d["tp"], full[d["tp_rows"]])
         _close("fused", d["fused"], full[d["fused_rows"]])
         _close("m-shard", d["m"], full[int(d["m_lo"]):int(d["m_hi"])], floor=1e-3)
+
+
+def _dead_rank_worker(rank, world, port, out_dir):
+    """Rank 1 leaves between steps (launches nothing for step 2, no kernel or collective in
+    flight); rank 0's band owners wait for partials that never come, their bounded wait runs
+    out, the kernel reports a peer timeout and returns; the ranks meet again on the host,
+    reset together and run a correct step."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from ffn_optim_b200.sharded import FusedTensorParallelFFN
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        x, w1, w2 = (t.to(dev) for t in _inputs())
+        fused = FusedTensorParallelFFN(x, w1, w2)
+        fused.prepared.set_wait_limit(0.5)
+        good = fused.run().clone()
+        fused.check()
+        dist.barrier()
+        status = [0, 0, 0, 0]
+        if rank == 0:
+            fused.run()
+            status = fused.prepared.status()  # synchronises: the kernel has returned
+        dist.barrier()
+        fused.prepared.reset()  # every rank clears its counts and restarts its epoch
+        torch.cuda.synchronize()
+        dist.barrier()
+        again = fused.run().clone()
+        fused.check()
+        np.savez(os.path.join(out_dir, f"dead{rank}.npz"), status=np.array(status),
+                 same=bool(torch.equal(good, again)))
+        fused.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_reduce_scatter_detects_missing_rank(tmp_path):
+    mp.spawn(_dead_rank_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    d0 = np.load(tmp_path / "dead0.npz")
+    assert int(d0["status"][0]) == 4, d0["status"]  # FFN_B200_KERNEL_PEER_TIMEOUT
+    for r in range(2):
+        assert bool(np.load(tmp_path / f"dead{r}.npz")["same"])
