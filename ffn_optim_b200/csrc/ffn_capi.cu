@@ -227,7 +227,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   const int grid = pr->block_num > 0 ? pr->block_num : sm;
   if (grid < 1 || grid > 65535 || pr->block_num < 0) return FFN_B200_ERR_INVALID;
   if (pr->tile_variant < 0 || pr->tile_variant > kNumVariants) return FFN_B200_ERR_INVALID;
-  if (pr->raster_group < 0 || pr->l2_policy < 0 || pr->l2_policy > 2) return FFN_B200_ERR_INVALID;
+  if (pr->raster_group < 0 || pr->l2_policy < 0 || pr->l2_policy > 3) return FFN_B200_ERR_INVALID;
 
   std::memset(out, 0, sizeof(*out));
   int variant;
@@ -394,7 +394,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.C = plan.block_num / ncta;
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
-  P.l2_hints = prob.l2_policy == 2 ? 1 : 0;
+  P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : 0);
   // Readiness counters gain epi * ncta * (up tiles per row block) per launch, flags epi per launch.
   const int64_t per_blk = static_cast<int64_t>(kVariants[plan.variant].epi) * ncta * (sw ? plan.up.tiles_r : plan.up.tiles_q);
   h->epoch_limit = static_cast<unsigned>(((int64_t(1) << 30) / (per_blk > 4 ? per_blk : 4)));

@@ -78,7 +78,7 @@ struct Params {
   unsigned epoch;
   unsigned long long wait_limit_ns;
   int inject;
-  int l2_hints;          // 1: evict-last on A (row operand), evict-first on B (column operand)
+  int l2_hints;          // 1: evict-last on A (row operand), evict-first on B; 2: evict-normal on both
   unsigned long long* trace;  // optional [grid][8] %globaltimer stamps (see TraceSlot), null = off
   // Fused reduce-scatter of the down phase across `rs_world` GPUs (tensor parallel over H):
   // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
@@ -194,6 +194,11 @@ __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 __device__ __forceinline__ uint64_t policy_evict_last() {
@@ -655,8 +660,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
       const unsigned per_blk = static_cast<unsigned>(EPI * kNcta) * static_cast<unsigned>(SWAP ? p.up.tiles_r : p.up.tiles_q);
       const unsigned target = p.epoch * per_blk + (p.inject ? 1u : 0u);
       // Optional L2 policy (off by default: on cfg5 it raised DRAM reads from 62 GB to 430 GB).
-      const uint64_t pol_a = policy_evict_last();
-      const uint64_t pol_b = policy_evict_first();
+      const uint64_t pol_a = p.l2_hints == 2 ? policy_evict_normal() : policy_evict_last();
+      const uint64_t pol_b = p.l2_hints == 2 ? policy_evict_normal() : policy_evict_first();
       const bool hints = p.l2_hints != 0 && !SWAP;
       bool ok = true;
 #pragma unroll 1

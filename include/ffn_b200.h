@@ -87,7 +87,8 @@ typedef struct {
                             6: swap 16 with 256-wide K stages, 7: swap 64 with 128-wide K stages) */
   int32_t raster_group; /* tile rows per raster group (default: balances A and B bytes per wave) */
   int32_t l2_policy;    /* 1: no L2 eviction hints (default); 2: evict-last on the row operand and
-                           evict-first on the column operand (measured: far more DRAM traffic) */
+                           evict-first on the column operand (measured: far more DRAM traffic);
+                           3: explicit evict-normal hint on every operand load */
 } ffn_b200_problem;
 
 /* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
