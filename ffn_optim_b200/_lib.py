@@ -22,6 +22,7 @@ ERR_CUDA = 5
 ERR_ALIGNMENT = 6
 ERR_TOO_LARGE = 7
 ERR_SCRATCH = 8
+ERR_EPOCH = 9
 NOALLOC_SCRATCH_BYTES = 32 << 20
 
 DTYPES = {"float16": 0, "bfloat16": 1}
@@ -30,7 +31,7 @@ GELU_CODES = {"rational": 0, "erf": 1}
 # Kernel variants selectable through prepare_ffn(..., tile=...) (None = automatic).
 TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5,
                  "swap16k4": 6, "swap64k2": 7}
-L2_POLICIES = {"none": 1, "stream_b": 2, "normal": 3}
+L2_POLICIES = {"none": 1, "stream_b": 2, "normal": 3, "keep_a": 4}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",
                  3: "Stream-K partial wait timed out", 4: "peer GPU partial wait timed out (fused reduce-scatter)"}
 

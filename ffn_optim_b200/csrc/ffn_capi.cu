@@ -191,6 +191,7 @@ const char* ffn_b200_strerror(int code) {
     case FFN_B200_ERR_CUDA: return "CUDA call failed";
     case FFN_B200_ERR_ALIGNMENT: return "buffer base not 16-byte aligned or pitch not a multiple of 8 elements";
     case FFN_B200_ERR_TOO_LARGE: return "problem does not fit one launch";
+    case FFN_B200_ERR_EPOCH: return "launch epoch exhausted: reset every rank of the reduce-scatter together";
     case FFN_B200_ERR_SCRATCH:
       return "problem needs more scratch than the 32 MiB that ffn_b200_run_noalloc holds; use ffn_b200_prepare";
   }
@@ -227,7 +228,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   const int grid = pr->block_num > 0 ? pr->block_num : sm;
   if (grid < 1 || grid > 65535 || pr->block_num < 0) return FFN_B200_ERR_INVALID;
   if (pr->tile_variant < 0 || pr->tile_variant > kNumVariants) return FFN_B200_ERR_INVALID;
-  if (pr->raster_group < 0 || pr->l2_policy < 0 || pr->l2_policy > 3) return FFN_B200_ERR_INVALID;
+  if (pr->raster_group < 0 || pr->l2_policy < 0 || pr->l2_policy > 4) return FFN_B200_ERR_INVALID;
 
   std::memset(out, 0, sizeof(*out));
   int variant;
@@ -394,7 +395,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.C = plan.block_num / ncta;
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
-  P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : 0);
+  P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : (prob.l2_policy == 4 ? 3 : 0));
   // Readiness counters gain epi * ncta * (up tiles per row block) per launch, flags epi per launch.
   const int64_t per_blk = static_cast<int64_t>(kVariants[plan.variant].epi) * ncta * (sw ? plan.up.tiles_r : plan.up.tiles_q);
   h->epoch_limit = static_cast<unsigned>(((int64_t(1) << 30) / (per_blk > 4 ? per_blk : 4)));
@@ -464,6 +465,9 @@ int ffn_b200_run(ffn_b200_handle* h, void* stream) {
   if (!h) return FFN_B200_ERR_INVALID;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (h->epoch + 1 >= h->epoch_limit) {
+    // Under the fused reduce-scatter the counts live partly in other GPUs' memory: all ranks
+    // must reset together at a quiescent point, so the caller is told instead.
+    if (h->params.rs_world > 1) return FFN_B200_ERR_EPOCH;
     const int rc = ffn_b200_reset(h, stream);
     if (rc) return rc;
   }

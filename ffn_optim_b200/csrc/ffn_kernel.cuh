@@ -78,7 +78,8 @@ struct Params {
   unsigned epoch;
   unsigned long long wait_limit_ns;
   int inject;
-  int l2_hints;          // 1: evict-last on A (row operand), evict-first on B; 2: evict-normal on both
+  int l2_hints;          // 1: evict-last on A (row operand), evict-first on B; 2: evict-normal on
+                         // both; 3: evict-last on A only
   unsigned long long* trace;  // optional [grid][8] %globaltimer stamps (see TraceSlot), null = off
   // Fused reduce-scatter of the down phase across `rs_world` GPUs (tensor parallel over H):
   // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
@@ -663,6 +664,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
       const uint64_t pol_a = p.l2_hints == 2 ? policy_evict_normal() : policy_evict_last();
       const uint64_t pol_b = p.l2_hints == 2 ? policy_evict_normal() : policy_evict_first();
       const bool hints = p.l2_hints != 0 && !SWAP;
+      const bool hint_b = p.l2_hints != 3;  // policy 3: hint only the row operand (A)
       bool ok = true;
 #pragma unroll 1
       for (int idx = 0; ok; ++idx) {
@@ -682,12 +684,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
           for (int j = 0; j < KSUB; ++j) {
             const uint32_t dst = which == 0 ? sA + st * LY::kAStage + j * kABytes : sB + st * LY::kBStage + j * LY::kBSub;
             const int kx = (kb * KSUB + j) * kBK;
+            const bool hinted = hints && (which == 0 || hint_b);
             if constexpr (PAIR) {
               const uint32_t fb = map_to_rank(full_bar(st), 0);
-              if (hints) tma_load_2d_pair_hint(dst, tm, kx, row, fb, which == 0 ? pol_a : pol_b);
+              if (hinted) tma_load_2d_pair_hint(dst, tm, kx, row, fb, which == 0 ? pol_a : pol_b);
               else tma_load_2d_pair(dst, tm, kx, row, fb);
             } else {
-              if (hints) tma_load_2d_hint(dst, tm, kx, row, full_bar(st), which == 0 ? pol_a : pol_b);
+              if (hinted) tma_load_2d_hint(dst, tm, kx, row, full_bar(st), which == 0 ? pol_a : pol_b);
               else tma_load_2d(dst, tm, kx, row, full_bar(st));
             }
           }

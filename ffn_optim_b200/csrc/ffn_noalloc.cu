@@ -160,7 +160,7 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   P.epoch = 1;
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
-  P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : 0);
+  P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : (prob.l2_policy == 4 ? 3 : 0));
 
   cudaStream_t sh = static_cast<cudaStream_t>(stream);
   // Everything the kernel counts from zero starts at zero: counters, flags, status.

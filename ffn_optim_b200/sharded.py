@@ -285,8 +285,26 @@ class FusedTensorParallelFFN:
         return 1
 
     def run(self):
-        self.prepared.run()
+        from .api import EpochExhausted
+
+        try:
+            self.prepared.run()
+        except EpochExhausted:
+            self.collective_reset()
+            self.prepared.run()
         return self.y[:, :self.n]
+
+    def collective_reset(self):
+        """Every rank clears its push counts and restarts its launch epoch, at a point where
+        no rank has a kernel in flight (all ranks call this together)."""
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.prepared.reset()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
 
     def local_rows(self):
         per = self.m // self.world
@@ -304,3 +322,9 @@ class FusedTensorParallelFFN:
         for ptr in getattr(self, "_own", []):
             lib.ffn_b200_peer_free(ptr)
         self._opened, self._own = [], []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass

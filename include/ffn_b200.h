@@ -47,7 +47,8 @@ typedef enum {
   FFN_B200_ERR_CUDA = 5,           /* a CUDA runtime / driver call failed */
   FFN_B200_ERR_ALIGNMENT = 6,      /* base not 16-byte aligned or pitch not a multiple of 8 elements */
   FFN_B200_ERR_TOO_LARGE = 7,      /* tile count does not fit one launch */
-  FFN_B200_ERR_SCRATCH = 8         /* needs more scratch than ffn_b200_run_noalloc holds */
+  FFN_B200_ERR_SCRATCH = 8,        /* needs more scratch than ffn_b200_run_noalloc holds */
+  FFN_B200_ERR_EPOCH = 9           /* reduce-scatter handle needs a collective reset (after ~2^30/tiles runs) */
 } ffn_b200_status;
 
 typedef enum { FFN_B200_F16 = 0, FFN_B200_BF16 = 1 } ffn_b200_dtype;
@@ -88,7 +89,8 @@ typedef struct {
   int32_t raster_group; /* tile rows per raster group (default: balances A and B bytes per wave) */
   int32_t l2_policy;    /* 1: no L2 eviction hints (default); 2: evict-last on the row operand and
                            evict-first on the column operand (measured: far more DRAM traffic);
-                           3: explicit evict-normal hint on every operand load */
+                           3: explicit evict-normal hint on every operand load;
+                           4: evict-last on the row operand only */
 } ffn_b200_problem;
 
 /* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
