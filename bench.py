@@ -47,6 +47,8 @@ def parse():
                          "fused into the kernel (NVLink peer stores), m = M-sharded")
     ap.add_argument("--chunks", type=int, default=4)
     ap.add_argument("--tile", default=None, help="force a kernel variant (see ffn_optim_b200._lib.TILE_VARIANTS)")
+    ap.add_argument("--schedule", choices=("static", "dynamic"), default=None,
+                    help="data-parallel tile order (default: dynamic for CTA-pair tiles, static otherwise)")
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--flush", choices=("auto", "on", "off"), default="auto",
                     help="flush L2 between timed steps (auto: when the operands fit in 2x L2)")
@@ -273,7 +275,7 @@ def main():
     down = case.get("down_impl", "basic")
 
     if world == 1:
-        runner = prepare_ffn(x, w1, w2, down_impl=down, tile=args.tile)
+        runner = prepare_ffn(x, w1, w2, down_impl=down, tile=args.tile, schedule=args.schedule)
         launches = 1
         kernel_runs = lambda: runner.run()  # noqa: E731
         check = runner.check
@@ -297,7 +299,7 @@ def main():
     else:
         from ffn_optim_b200.sharded import RowShardedFFN
 
-        runner = RowShardedFFN(x, w1, w2, down_impl=down, tile=args.tile)
+        runner = RowShardedFFN(x, w1, w2, down_impl=down, tile=args.tile, schedule=args.schedule)
         launches = 1
         kernel_runs = runner.run
         check = runner.check
@@ -405,6 +407,7 @@ def main():
                 "config": {"workload": args.workload, "x": list(p.input_shape), "w1": [p.h, p.k], "w2": [p.n, p.h],
                            "down_impl": down, "parallelism": parallelism,
                            "block_num": block_num, "kernel_variant": variant,
+                           "schedule": {1: "static", 2: "dynamic"}.get(first.plan.kernel.get("schedule")),
                            "l2": "L2 flushed between steps (512 MB write)" if flush else "inputs larger than L2, no flush"},
                 "gpu_launches": launches * args.steps, "clocks": clocks, "roofline": roofline,
                 "e2e": e2e, "cpu_baseline": cpu}

@@ -32,13 +32,16 @@ GELU_CODES = {"rational": 0, "erf": 1}
 TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5,
                  "swap16k4": 6, "swap64k2": 7}
 L2_POLICIES = {"none": 1, "stream_b": 2, "normal": 3, "keep_a": 4}
+SCHEDULES = {"static": 1, "dynamic": 2}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",
-                 3: "Stream-K partial wait timed out", 4: "peer GPU partial wait timed out (fused reduce-scatter)"}
+                 3: "Stream-K partial wait timed out", 4: "peer GPU partial wait timed out (fused reduce-scatter)",
+                 5: "tile claim out of range (counters not reset after an earlier error)"}
 
 # Every symbol the header declares; the CPU tests check the library exports all of them.
 EXPORTED = ("ffn_b200_abi_version", "ffn_b200_strerror", "ffn_b200_device_info", "ffn_b200_make_plan",
             "ffn_b200_prepare", "ffn_b200_run", "ffn_b200_rebind_io", "ffn_b200_reset",
-            "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_set_trace", "ffn_b200_get_plan",
+            "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_set_trace",
+            "ffn_b200_set_owner_map", "ffn_b200_get_owner_map", "ffn_b200_get_plan",
             "ffn_b200_destroy", "ffn_b200_launch", "ffn_b200_run_noalloc", "ffn_b200_peer_alloc",
             "ffn_b200_peer_open", "ffn_b200_peer_close", "ffn_b200_peer_free", "ffn_b200_reduce_scatter_bytes",
             "ffn_b200_set_reduce_scatter")
@@ -48,7 +51,7 @@ class Problem(ctypes.Structure):
     _fields_ = [("m", ctypes.c_int64), ("k", ctypes.c_int64), ("h", ctypes.c_int64), ("n", ctypes.c_int64),
                 ("dtype", ctypes.c_int32), ("down_impl", ctypes.c_int32), ("gelu", ctypes.c_int32),
                 ("block_num", ctypes.c_int32), ("sm_count", ctypes.c_int32), ("tile_variant", ctypes.c_int32),
-                ("raster_group", ctypes.c_int32), ("l2_policy", ctypes.c_int32)]
+                ("raster_group", ctypes.c_int32), ("l2_policy", ctypes.c_int32), ("schedule", ctypes.c_int32)]
 
 
 class PhasePlan(ctypes.Structure):
@@ -67,7 +70,7 @@ class PlanInfo(ctypes.Structure):
                 ("block_num", ctypes.c_int32), ("tmem_cols", ctypes.c_int32), ("smem_bytes", ctypes.c_int64),
                 ("up", PhasePlan), ("down", PhasePlan), ("workspace_floats", ctypes.c_int64),
                 ("counter_words", ctypes.c_int64), ("flag_words", ctypes.c_int64),
-                ("status_words", ctypes.c_int64)]
+                ("status_words", ctypes.c_int64), ("schedule", ctypes.c_int32)]
 
     def to_dict(self):
         out = {}
@@ -122,6 +125,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             "ffn_b200_set_wait_limit": ([vp, u64], i32),
             "ffn_b200_set_fault_injection": ([vp, i32], i32),
             "ffn_b200_set_trace": ([vp, vp], i32),
+            "ffn_b200_set_owner_map": ([vp, vp], i32),
+            "ffn_b200_get_owner_map": ([vp, vp, i32, vp], i32),
             "ffn_b200_get_plan": ([vp, ctypes.POINTER(PlanInfo)], i32),
             "ffn_b200_destroy": ([vp], i32),
             "ffn_b200_launch": ([ctypes.POINTER(Problem), ctypes.POINTER(Buffers), vp], i32),

@@ -14,7 +14,7 @@ from time import perf_counter
 from . import _lib
 from .host.dispatch import Selection, kernel_provenance
 from .host.inputs import prepare_storage, validate_tensors
-from .host.tiling import make_plan
+from .host.tiling import make_plan, problem_struct
 
 
 class KernelCompilationError(RuntimeError):
@@ -94,12 +94,11 @@ class PreparedFFN:
         while lo < p.m:
             hi = min(p.m, lo + rows)
             sub = self.plan.problem.__class__((hi - lo, p.k), hi - lo, p.k, p.h, p.n, p.dtype, p.layout)
-            from .host.tiling import make_plan
-
             o = self.plan.kernel.get("overrides", {})
-            plan = make_plan(sub, self.plan.selection, self.plan.block_num, gelu=self.plan.gelu,
-                             sm_count=torch.cuda.get_device_properties(dev).multi_processor_count,
-                             tile=o.get("tile"), raster_group=o.get("raster_group"), l2_policy=o.get("l2_policy"))
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            plan = make_plan(sub, self.plan.selection, self.plan.block_num, gelu=self.plan.gelu, sm_count=sms,
+                             tile=o.get("tile"), raster_group=o.get("raster_group"), l2_policy=o.get("l2_policy"),
+                             schedule=o.get("schedule"))
             k = plan.kernel
             if k["workspace_floats"] > ws.numel():
                 ws = torch.empty(int(k["workspace_floats"]), dtype=torch.float32, device=dev)
@@ -108,11 +107,8 @@ class PreparedFFN:
             bufs = _lib.Buffers(x2d[lo].data_ptr(), x2d.stride(0), w1.data_ptr(), w1.stride(0), w2.data_ptr(),
                                 w2.stride(0), hidden[lo].data_ptr(), hidden.stride(0), out[lo].data_ptr(),
                                 out.stride(0), ws.data_ptr(), cnt.data_ptr(), flg.data_ptr(), st.data_ptr())
-            prob = _lib.Problem(hi - lo, p.k, p.h, p.n, _lib.DTYPES[p.dtype],
-                                _lib.DOWN_IMPL_CODES[self.plan.selection.down_impl], _lib.GELU_CODES[self.plan.gelu],
-                                plan.block_num, torch.cuda.get_device_properties(dev).multi_processor_count,
-                                _lib.TILE_VARIANTS[o["tile"]] if o.get("tile") else 0, int(o.get("raster_group") or 0),
-                                _lib.L2_POLICIES[o["l2_policy"]] if o.get("l2_policy") else 0)
+            prob = problem_struct(sub, self.plan.selection.down_impl, self.plan.gelu, plan.block_num, sms,
+                                  o.get("tile"), o.get("raster_group"), o.get("l2_policy"), o.get("schedule"))
             h = ctypes.c_void_p()
             rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), dev.index or 0, ctypes.byref(h))
             if rc != _lib.OK:
@@ -217,11 +213,12 @@ class PreparedFFN:
 
     def trace(self):
         """Runs once with per-CTA %globaltimer stamps and returns a dict of phase times (us)
-        relative to the earliest setup stamp: per-slot min/median/max over CTAs."""
+        relative to the earliest setup stamp: per-slot min/median/max over CTAs, and under
+        "smid" the SM each CTA ran on (index = CTA)."""
         import torch
 
         grid = self.plan.block_num
-        stamps = torch.zeros((grid, 8), dtype=torch.int64, device=self.storage[0].device)
+        stamps = torch.zeros((grid, 16), dtype=torch.int64, device=self.storage[0].device)
         lib = _lib.load()
         if lib.ffn_b200_set_trace(self.handle, stamps.data_ptr()) != _lib.OK:
             raise RuntimeError("ffn_b200_set_trace failed")
@@ -240,7 +237,39 @@ class PreparedFFN:
                 rel = (col - t0) / 1e3
                 out[name] = {"min": float(rel.min()), "median": float(rel.median()), "max": float(rel.max()),
                              "ctas": int(col.numel())}
+        out["smid"] = [int(v) for v in t[:, 8]]
         return out
+
+    def set_owner_map(self, owners):
+        """Work-list index of each CTA (CTA pair for pair tiles): a permutation of
+        0..C-1, or None for launch order.  Only the tile-to-SM placement changes; every
+        tile is still computed once by the same arithmetic."""
+        import torch
+
+        lib = _lib.load()
+        if owners is None:
+            self._owner_map = None
+            rc = lib.ffn_b200_set_owner_map(self.handle, None)
+        else:
+            n = self.plan.block_num // (2 if self.plan.kernel["cta_pair"] else 1)
+            owners = [int(v) for v in owners]
+            if sorted(owners) != list(range(n)):
+                raise ValueError(f"owner map must be a permutation of 0..{n - 1}")
+            self._owner_map = torch.tensor(owners, dtype=torch.int32, device=self.storage[0].device)
+            rc = lib.ffn_b200_set_owner_map(self.handle, self._owner_map.data_ptr())
+        if rc != _lib.OK:
+            raise RuntimeError(f"ffn_b200_set_owner_map: {_lib.strerror(rc)}")
+
+    def owner_map(self):
+        """The work-list index of each CTA (pair) in use, or None for launch order."""
+        lib = _lib.load()
+        cap = 1024
+        buf = (ctypes.c_int32 * cap)()
+        count = ctypes.c_int32(0)
+        rc = lib.ffn_b200_get_owner_map(self.handle, buf, cap, ctypes.byref(count))
+        if rc != _lib.OK:
+            raise RuntimeError(f"ffn_b200_get_owner_map: {_lib.strerror(rc)}")
+        return [int(v) for v in buf[:count.value]] if count.value else None
 
     def close(self):
         if self.handle is not None:
@@ -267,16 +296,16 @@ def _map_prepare_error(rc):
 
 
 def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", block_num=None,
-                layout="linear", gelu="rational", tile=None, raster_group=None, l2_policy=None):
+                layout="linear", gelu="rational", tile=None, raster_group=None, l2_policy=None, schedule=None):
     """Validates, plans and prepares storage and the launch handle without launching the FFN
     (reference ops/api.py:48-89).
 
     ``block_num`` is the persistent CTA count, at most the device's SM count (default: all
     SMs).  ``gelu`` selects the epilogue GELU: 'rational' (the reference kernel's clipped
     rational erf) or 'erf' (CUDA ``erff``).  ``tile`` forces a kernel variant (see
-    ``make_plan``); None chooses automatically; ``raster_group`` and ``l2_policy`` are
-    tuning overrides passed to ``make_plan``.  Storage copies are device work timed
-    separately as ``preparation['auxiliary_device_interval_ms']``.
+    ``make_plan``); None chooses automatically; ``raster_group``, ``l2_policy`` and
+    ``schedule`` are tuning overrides passed to ``make_plan``.  Storage copies are device
+    work timed separately as ``preparation['auxiliary_device_interval_ms']``.
     """
     import torch
 
@@ -288,7 +317,7 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
         raise KernelCompilationError(f"{type(exc).__name__}: {exc}") from exc
     props = torch.cuda.get_device_properties(x.device)
     plan = make_plan(p, selection, block_num, gelu=gelu, sm_count=props.multi_processor_count, tile=tile,
-                     raster_group=raster_group, l2_policy=l2_policy)
+                     raster_group=raster_group, l2_policy=l2_policy, schedule=schedule)
     if (props.major, props.minor) != (10, 0):
         raise RuntimeError("This implementation targets B200 (sm_100) only")
     if plan.block_num > props.multi_processor_count:
@@ -305,10 +334,8 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
         bufs = _lib.Buffers(x2d.data_ptr(), x2d.stride(0), w1.data_ptr(), w1.stride(0), w2.data_ptr(), w2.stride(0),
                             hidden.data_ptr(), hidden.stride(0), out.data_ptr(), out.stride(0), ws.data_ptr(),
                             counters.data_ptr(), flags.data_ptr(), status.data_ptr())
-        prob = _lib.Problem(p.m, p.k, p.h, p.n, _lib.DTYPES[p.dtype], _lib.DOWN_IMPL_CODES[down_impl],
-                            _lib.GELU_CODES[gelu], plan.block_num, props.multi_processor_count,
-                            _lib.TILE_VARIANTS[tile] if tile else 0, int(raster_group or 0),
-                            _lib.L2_POLICIES[l2_policy] if l2_policy else 0)
+        prob = problem_struct(p, down_impl, gelu, plan.block_num, props.multi_processor_count, tile, raster_group,
+                              l2_policy, schedule)
         handle = ctypes.c_void_p()
         before = perf_counter()
         rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), x.device.index or 0, ctypes.byref(handle))

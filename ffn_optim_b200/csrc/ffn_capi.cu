@@ -20,6 +20,10 @@
 #include "../../include/ffn_b200.h"
 #include "ffn_kernel.cuh"
 
+namespace ffnb200 {
+const int32_t* internal_pair_owner_map(int device, int grid, int smem);  // ffn_placement.cu
+}  // namespace ffnb200
+
 namespace {
 
 using ffnb200::Params;
@@ -229,6 +233,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   if (grid < 1 || grid > 65535 || pr->block_num < 0) return FFN_B200_ERR_INVALID;
   if (pr->tile_variant < 0 || pr->tile_variant > kNumVariants) return FFN_B200_ERR_INVALID;
   if (pr->raster_group < 0 || pr->l2_policy < 0 || pr->l2_policy > 4) return FFN_B200_ERR_INVALID;
+  if (pr->schedule < 0 || pr->schedule > 2) return FFN_B200_ERR_INVALID;
 
   std::memset(out, 0, sizeof(*out));
   int variant;
@@ -300,9 +305,15 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   out->tmem_cols = tmem_cols_for(variant);
   out->smem_bytes = smem_for(variant);
   out->workspace_floats = 2ll * C * ncta * ffnb200::kBM * v.bn;
-  out->counter_words = v.swap ? out->up.tiles_q : out->up.tiles_r;
+  out->counter_words = ffnb200::kClaimWords + (v.swap ? out->up.tiles_q : out->up.tiles_r);
   out->flag_words = 2ll * C * ncta;
   out->status_words = 4;
+  // Automatic: dynamic claims for CTA-pair plans, whose pairs drift apart under the static
+  // order (cfg5: 773 us of spread at the phase change, 189 GB of DRAM reads against 93 GB
+  // dynamic); static for one-CTA tiles, whose cooperative launch keeps GPC-major placement
+  // and little drift (cfg5: 52 GB static against 64 GB dynamic) and for decode grids of one
+  // or two waves, where a claim would only add its latency.
+  out->schedule = pr->schedule ? pr->schedule : (v.pair ? 2 : 1);
   return FFN_B200_OK;
 }
 
@@ -328,6 +339,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   for (const void* p : bases)
     if (!aligned16(p)) return FFN_B200_ERR_ALIGNMENT;
   if (!b->counters || !b->flags || !b->status) return FFN_B200_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(b->counters) & 7u) return FFN_B200_ERR_ALIGNMENT;
   const int64_t pitches[] = {b->ldx, b->ldw1, b->ldw2, b->ldh, b->ldy};
   for (int64_t p : pitches)
     if (p <= 0 || (p % 8) != 0) return FFN_B200_ERR_ALIGNMENT;
@@ -376,7 +388,9 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.ldh = b->ldh;
   P.ldy = b->ldy;
   P.ws = b->workspace;
-  P.counters = b->counters;
+  P.claims = reinterpret_cast<unsigned long long*>(b->counters);
+  P.counters = b->counters + ffnb200::kClaimWords;
+  P.dyn = plan.schedule == 2 ? 1 : 0;
   P.flags = b->flags;
   P.status = b->status;
   auto to_sched = [](const ffn_b200_phase_plan& pp) {
@@ -429,6 +443,10 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
       rc2 = FFN_B200_ERR_DEVICE;
     }
   }
+  // Pair plans over the whole GPU: renumber the pairs so that neighbouring work-list owners
+  // share a GPC (see ffn_placement.cu); null keeps launch order.
+  if (!rc2 && plan.cta_pair)
+    P.owner_map = ffnb200::internal_pair_owner_map(device, plan.block_num, static_cast<int>(plan.smem_bytes));
   if (cur != device) cudaSetDevice(cur);
   if (rc2) {
     cudaGetLastError();
@@ -627,6 +645,26 @@ int ffn_b200_set_trace(ffn_b200_handle* h, uint64_t* device_stamps) {
   if (!h) return FFN_B200_ERR_INVALID;
   if (device_stamps && (reinterpret_cast<uintptr_t>(device_stamps) & 7u)) return FFN_B200_ERR_ALIGNMENT;
   h->params.trace = reinterpret_cast<unsigned long long*>(device_stamps);
+  return FFN_B200_OK;
+}
+
+int ffn_b200_set_owner_map(ffn_b200_handle* h, const int32_t* device_map) {
+  if (!h) return FFN_B200_ERR_INVALID;
+  if (device_map && (reinterpret_cast<uintptr_t>(device_map) & 3u)) return FFN_B200_ERR_ALIGNMENT;
+  h->params.owner_map = device_map;
+  return FFN_B200_OK;
+}
+
+int ffn_b200_get_owner_map(const ffn_b200_handle* h, int32_t* host_out, int32_t capacity, int32_t* count) {
+  if (!h || !count || capacity < 0 || (capacity > 0 && !host_out)) return FFN_B200_ERR_INVALID;
+  const int owners = h->plan.block_num / (h->plan.cta_pair ? 2 : 1);
+  *count = h->params.owner_map ? owners : 0;
+  if (!h->params.owner_map || capacity == 0) return FFN_B200_OK;
+  const int n = owners < capacity ? owners : capacity;
+  if (cudaMemcpy(host_out, h->params.owner_map, sizeof(int32_t) * n, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return FFN_B200_ERR_CUDA;
+  }
   return FFN_B200_OK;
 }
 

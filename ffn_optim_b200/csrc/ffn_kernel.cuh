@@ -80,7 +80,13 @@ struct Params {
   int inject;
   int l2_hints;          // 1: evict-last on A (row operand), evict-first on B; 2: evict-normal on
                          // both; 3: evict-last on A only
-  unsigned long long* trace;  // optional [grid][8] %globaltimer stamps (see TraceSlot), null = off
+  unsigned long long* trace;  // optional [grid][16]: TraceSlot stamps, then kTrSmid; null = off
+  const int* owner_map;       // optional [C]: work-list owner of each CTA (pair), a permutation of
+                              // 0..C-1; null = launch order
+  unsigned long long* claims;  // [2] per-phase counters of claimed data-parallel tiles; every
+                               // launch adds exactly dp + C (one failed claim per owner)
+  int dyn;                     // 1: data-parallel tiles are claimed from `claims` in raster order;
+                               // 0: owner c takes tiles c, c + C, ...
   // Fused reduce-scatter of the down phase across `rs_world` GPUs (tensor parallel over H):
   // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
   // of another rank's band is pushed as a bf16 partial into that rank's staging buffer over
@@ -93,6 +99,9 @@ struct Params {
 
 static_assert(sizeof(Params) <= 4096, "kernel parameters must fit the 4 KB parameter space");
 
+// u32 words at the start of the counters buffer that hold the two u64 tile-claim counters.
+constexpr int kClaimWords = 4;
+
 // Per-CTA trace stamps (ns, %globaltimer) written when Params::trace is set.
 enum TraceSlot : int {
   kTrStart = 0,       // setup done (barriers, TMEM)
@@ -102,7 +111,9 @@ enum TraceSlot : int {
   kTrLastMma = 4,     // MMA thread committed its last accumulator
   kTrUpStored = 5,    // first epilogue warp finished its last up-phase unit
   kTrFirstDown = 6,   // first epilogue warp got its first down-phase accumulator
-  kTrEnd = 7          // teardown reached
+  kTrEnd = 7,         // teardown reached
+  kTrSmid = 8,        // not a stamp: the SM (%smid) the CTA ran on
+  kTrWords = 16       // words per CTA
 };
 
 // ------------------------------------------------------------------------------------------
@@ -258,6 +269,42 @@ __device__ __forceinline__ void cluster_sync() {
 }
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Parity wait with acquire at cluster scope: for data that the other CTA of the pair wrote
+// into this CTA's shared memory (or read from it) before its release-arrive.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// 8 words to / from a shared-memory slot of this CTA, or (cluster address) of the peer CTA.
+__device__ __forceinline__ void st_shared_8(uint32_t addr, const int* v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3])
+               : "memory");
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr + 16), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster_8(uint32_t cluster_addr, const int* v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3])
+               : "memory");
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr + 16), "r"(v[4]), "r"(v[5]),
+               "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void ld_shared_8(uint32_t addr, int* v) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]) : "r"(addr)
+               : "memory");
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(addr + 16)
+               : "memory");
 }
 // TMA load into this CTA's shared memory whose completion is counted on an mbarrier of
 // either CTA of the pair (here: the leader's), no multicast.
@@ -462,42 +509,42 @@ __device__ __forceinline__ void unit_coords(const Params& p, const Unit& u, int&
   if (u.phase == 1 && p.rs_world > 1) tr = (tr + (p.rs_rank + 1) * p.rs_band_tiles) % s.tiles_r;
 }
 
-__device__ __forceinline__ bool get_unit(const Params& p, int c, int idx, Unit& u) {
-#pragma unroll 1
-  for (int ph = 0; ph < 2; ++ph) {
-    const PhaseSched& s = ph ? p.dn : p.up;
-    const int n_dp = c < s.dp ? (s.dp - c + p.C - 1) / p.C : 0;
-    if (idx < n_dp) {
-      u.phase = ph; u.tile = c + idx * p.C; u.kb0 = 0; u.kb1 = s.L;
-      u.role = kRoleFull; u.c_first = 1; u.c_last = 0;
-      return true;
-    }
-    idx -= n_dp;
-    int n_sk = 0, st = 0, en = 0;
-    if (s.sk > 0 && c < s.skc) {
-      st = sk_start(s, c);
-      en = sk_start(s, c + 1);
-      if (en > st) n_sk = (en - 1) / s.L - st / s.L + 1;
-    }
-    if (idx < n_sk) {
-      const int trel = st / s.L + idx;
-      const int tb = trel * s.L, te = tb + s.L;
-      const int a = max(st, tb), b = min(en, te);
-      u.phase = ph; u.tile = s.dp + trel; u.kb0 = a - tb; u.kb1 = b - tb;
-      if (a == tb) {
-        u.role = kRoleOwner; u.c_first = c + 1; u.c_last = sk_cta_of(s, te - 1);
-      } else {
-        u.role = kRoleContrib; u.c_first = 1; u.c_last = 0;
-      }
-      return true;
-    }
-    idx -= n_sk;
+// Data-parallel tile t of a phase: the whole K range in one unit.
+__device__ __forceinline__ void dp_unit(const PhaseSched& s, int ph, int t, Unit& u) {
+  u.phase = ph; u.tile = t; u.kb0 = 0; u.kb1 = s.L;
+  u.role = kRoleFull; u.c_first = 1; u.c_last = 0;
+}
+// Stream-K part `idx` of owner c in a phase (static split of the tail tiles' K blocks).
+__device__ __forceinline__ bool sk_unit(const PhaseSched& s, int ph, int c, int idx, Unit& u) {
+  if (s.sk <= 0 || c >= s.skc) return false;
+  const int st = sk_start(s, c);
+  const int en = sk_start(s, c + 1);
+  if (en <= st) return false;
+  const int n_sk = (en - 1) / s.L - st / s.L + 1;
+  if (idx >= n_sk) return false;
+  const int trel = st / s.L + idx;
+  const int tb = trel * s.L, te = tb + s.L;
+  const int a = max(st, tb), b = min(en, te);
+  u.phase = ph; u.tile = s.dp + trel; u.kb0 = a - tb; u.kb1 = b - tb;
+  if (a == tb) {
+    u.role = kRoleOwner; u.c_first = c + 1; u.c_last = sk_cta_of(s, te - 1);
+  } else {
+    u.role = kRoleContrib; u.c_first = 1; u.c_last = 0;
   }
-  return false;
+  return true;
+}
+// A unit as the 8 words of a unit-ring slot; word 7 = 1 for a unit, 0 for end of work.
+__device__ __forceinline__ void pack_unit(const Unit& u, int* w) {
+  w[0] = u.phase; w[1] = u.tile; w[2] = u.kb0; w[3] = u.kb1;
+  w[4] = u.role; w[5] = u.c_first; w[6] = u.c_last; w[7] = 1;
+}
+__device__ __forceinline__ void unpack_unit(const int* w, Unit& u) {
+  u.phase = w[0]; u.tile = w[1]; u.kb0 = w[2]; u.kb1 = w[3];
+  u.role = w[4]; u.c_first = w[5]; u.c_last = w[6];
 }
 
 __device__ __forceinline__ void trace_mark(const Params& p, int slot) {
-  if (p.trace) p.trace[static_cast<size_t>(blockIdx.x) * 8 + slot] = gtimer();
+  if (p.trace) p.trace[static_cast<size_t>(blockIdx.x) * kTrWords + slot] = gtimer();
 }
 
 __device__ __forceinline__ void report(const Params& p, int code, int aux) {
@@ -511,14 +558,16 @@ __device__ __forceinline__ void report(const Params& p, int code, int aux) {
 // On-chip pipeline waits get twice the limit of the cross-CTA waits below: when a readiness
 // counter or Stream-K flag never arrives, that wait (the cause) expires and reports first,
 // not the pipeline stages stalled behind it.
+template <bool CL = false>
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                          const Params& p, int aux) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto try_wait = [&]() { return CL ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+  if (try_wait()) return true;
   const uint64_t t0 = gtimer();
   uint32_t n = 0;
 #pragma unroll 1
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_wait()) return true;
     if ((++n & 15u) == 0) {
       if (*abort_flag) return false;
       if (gtimer() - t0 > 2 * p.wait_limit_ns) {
@@ -565,7 +614,15 @@ struct Layout {
   static constexpr int kStageBytes = kAStage + kBStage;
   static constexpr int kEpiBytes = SWAP ? 0 : EPI * 2 * kStageBufBytes;
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmem = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiBytes + kBarBytes;
+  // Unit ring: the leader's producer publishes each unit it takes (a claimed or static tile)
+  // for the MMA issuer, the epilogue warps and, in a pair, the peer CTA.  Deep enough that
+  // the producer (at most STAGES k-blocks ahead of the MMA, which is at most two
+  // accumulators ahead of the epilogue) never waits on it in steady state.
+  static constexpr int kRing = 16;
+  static constexpr int kRingBytes = kRing * 32 + 2 * kRing * 8;  // slots, full and empty barriers
+  static constexpr int kRingConsumers = PAIR ? 2 + 2 * EPI : 1 + EPI;  // MMA + epilogue warps (+ peer's producer and epilogue)
+  static constexpr int kSmem = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiBytes + kBarBytes + kRingBytes;
+  static_assert(kSmem <= 232448, "dynamic shared memory per CTA");
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static_assert((kBSub % 1024) == 0, "B tile must be whole swizzle atoms");
   static_assert((2 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");
@@ -608,12 +665,17 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
   const uint32_t drain_bar = sBar + 8u * (2 * STAGES + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (sBar - base) + 8 * (2 * STAGES + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t sRing = sBar + LY::kBarBytes;
+  auto ring_slot = [&](int i) { return sRing + 32u * i; };
+  auto ring_full = [&](int i) { return sRing + 32u * LY::kRing + 8u * i; };
+  auto ring_empty = [&](int i) { return sRing + 32u * LY::kRing + 8u * (LY::kRing + i); };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;
   const bool leader = rank == 0;
-  const int cta = static_cast<int>(blockIdx.x) / kNcta;  // work-list owner (one per tile-sized group)
+  // Work-list owner (one per tile-sized group of CTAs).
+  const int cta = p.owner_map ? p.owner_map[blockIdx.x / kNcta] : static_cast<int>(blockIdx.x) / kNcta;
   const int slot_base = static_cast<int>(rank);          // partial / flag slot = (phase*C + cta)*kNcta + rank
 
   if (threadIdx.x == 0) {
@@ -627,6 +689,11 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
       mbar_init(tempty_bar(a), 32 * EPI * kNcta);
     }
     mbar_init(drain_bar, 1);
+#pragma unroll 1
+    for (int i = 0; i < LY::kRing; ++i) {
+      mbar_init(ring_full(i), 1);
+      mbar_init(ring_empty(i), LY::kRingConsumers);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     fence_async_shared();
@@ -649,7 +716,14 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
   if constexpr (PAIR) cluster_sync();  // peer barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (threadIdx.x == 0) trace_mark(p, kTrStart);
+  if (threadIdx.x == 0) {
+    trace_mark(p, kTrStart);
+    if (p.trace) {
+      uint32_t smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      p.trace[static_cast<size_t>(blockIdx.x) * kTrWords + kTrSmid] = smid;
+    }
+  }
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -665,11 +739,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
       const uint64_t pol_b = p.l2_hints == 2 ? policy_evict_normal() : policy_evict_first();
       const bool hints = p.l2_hints != 0 && !SWAP;
       const bool hint_b = p.l2_hints != 3;  // policy 3: hint only the row operand (A)
-      bool ok = true;
-#pragma unroll 1
-      for (int idx = 0; ok; ++idx) {
-        Unit u;
-        if (!get_unit(p, cta, idx, u)) break;
+      // Issues the TMA loads of one unit; false when the CTA aborts.
+      auto do_loads = [&](const Unit& u) -> bool {
         int tr, tq;
         unit_coords(p, u, tr, tq);
         const CUtensorMap* ta = u.phase ? &p.tm_a_dn : &p.tm_a_up;
@@ -716,15 +787,14 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
             const int st0 = stage;
             int pre = 0;
             for (; pre < n_pre; ++pre) {
-              if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) { ok = false; break; }
+              if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) return false;
               arm(stage);
               load(wop, stage, kb + pre);
               if (issued == 0) trace_mark(p, kTrFirstLoad);
               ++issued;
               if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
-            if (!ok) break;
-            if (!wait_word_ge(p.counters + blk, target, abort_flag, p, 2, blk)) { ok = false; break; }
+            if (!wait_word_ge(p.counters + blk, target, abort_flag, p, 2, blk)) return false;
             fence_async_global();
             if (ready_blk < 0) trace_mark(p, kTrDownReady);
             ready_blk = blk;
@@ -734,13 +804,104 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
         }
 #pragma unroll 1
         for (; kb < u.kb1; ++kb) {
-          if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) { ok = false; break; }
+          if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) return false;
           arm(stage);
           load(0, stage, kb);
           load(1, stage, kb);
           if (issued == 0) trace_mark(p, kTrFirstLoad);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        return true;
+      };
+      bool ok = true;
+      int seq = 0;  // units published (leader) or taken from the ring (peer)
+      if (leader) {
+        // Publish a unit (8 words) in this CTA's ring slot and, in a pair, the peer's.
+        auto publish = [&](const int* w) -> bool {
+          const int slot = seq % LY::kRing;
+          const uint32_t par = static_cast<uint32_t>((seq / LY::kRing) & 1);
+          if (!wait_bar<PAIR>(ring_empty(slot), par ^ 1u, abort_flag, p, 500 + slot)) return false;
+          st_shared_8(ring_slot(slot), w);
+          if constexpr (PAIR) {
+            st_cluster_8(map_to_rank(ring_slot(slot), 1), w);
+            mbar_arrive_cluster(map_to_rank(ring_full(slot), 1));
+          }
+          mbar_arrive(ring_full(slot));
+          ++seq;
+          return true;
+        };
+#pragma unroll 1
+        for (int ph = 0; ph < 2 && ok; ++ph) {
+          const PhaseSched& s = ph ? p.dn : p.up;
+          // Data-parallel tiles.  Owner c's first tile is tile c; under the dynamic schedule
+          // every later one is claimed (tile C + claim index) so that the tiles in flight
+          // stay a contiguous stretch of the raster however far the owners drift apart.
+          // Every owner ends with one failed claim, so each launch advances the counter by
+          // exactly max(dp - C, 0) + C.  The next claim is in flight during the loads.
+          const long long span = max(s.dp - p.C, 0) + p.C;
+          const unsigned long long base = static_cast<unsigned long long>(p.epoch - 1u) * span;
+          const long long t_end = max(s.dp, p.C) + p.C;  // claimed tiles lie in [C, t_end)
+          auto claimed = [&](unsigned long long raw) { return p.C + static_cast<long long>(raw - base); };
+          long long t = cta;
+          bool from_claim = false;
+          if (p.dyn && t >= s.dp) {
+            t = claimed(atomicAdd(p.claims + ph, 1ull));
+            from_claim = true;
+          }
+#pragma unroll 1
+          while (true) {
+            if (from_claim && (t < p.C || t >= t_end)) {  // counters not reset after an error
+              report(p, 5, ph);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            if (t >= s.dp) break;
+            Unit u;
+            dp_unit(s, ph, static_cast<int>(t), u);
+            int w[8];
+            pack_unit(u, w);
+            if (!publish(w)) { ok = false; break; }
+            unsigned long long next = 0;
+            if (p.dyn) next = atomicAdd(p.claims + ph, 1ull);
+            if (!do_loads(u)) { ok = false; break; }
+            if (p.dyn) {
+              t = claimed(next);
+              from_claim = true;
+            } else {
+              t += p.C;
+            }
+          }
+          // Stream-K parts of this owner.
+#pragma unroll 1
+          for (int i = 0; ok; ++i) {
+            Unit u;
+            if (!sk_unit(s, ph, cta, i, u)) break;
+            int w[8];
+            pack_unit(u, w);
+            if (!publish(w) || !do_loads(u)) ok = false;
+          }
+        }
+        if (ok) {
+          const int w[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // end of work
+          ok = publish(w);
+        }
+      } else {
+        // The peer of a pair loads its halves of the units its leader publishes.
+#pragma unroll 1
+        while (ok) {
+          const int slot = seq % LY::kRing;
+          const uint32_t par = static_cast<uint32_t>((seq / LY::kRing) & 1);
+          if (!wait_bar<PAIR>(ring_full(slot), par, abort_flag, p, 600 + slot)) { ok = false; break; }
+          int w[8];
+          ld_shared_8(ring_slot(slot), w);
+          mbar_arrive_cluster(map_to_rank(ring_empty(slot), 0));
+          ++seq;
+          if (!w[7]) break;
+          Unit u;
+          unpack_unit(w, u);
+          if (!do_loads(u)) ok = false;
         }
       }
       trace_mark(p, kTrLastLoad);
@@ -771,9 +932,17 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
       uint32_t acc_phase = 0;
       bool ok = true;
 #pragma unroll 1
-      for (int idx = 0; ok; ++idx) {
+      for (int seq = 0; ok; ++seq) {
+        const int slot = seq % LY::kRing;
+        if (!wait_bar<PAIR>(ring_full(slot), static_cast<uint32_t>((seq / LY::kRing) & 1), abort_flag, p,
+                            600 + slot))
+          break;
+        int w[8];
+        ld_shared_8(ring_slot(slot), w);
+        mbar_arrive(ring_empty(slot));
+        if (!w[7]) break;
         Unit u;
-        if (!get_unit(p, cta, idx, u)) break;
+        unpack_unit(w, u);
         if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, p, 200 + acc)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -830,12 +999,31 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
     int sbuf = 0;
     bool seen_down = false;
 #pragma unroll 1
-    for (int idx = 0;; ++idx) {
+    for (int seq = 0;; ++seq) {
+      // Next unit from the ring: lane 0 waits, the warp reads the slot, lane 0 frees it.
+      const int slot = seq % LY::kRing;
+      int ok = 1;
+      if (lane == 0)
+        ok = wait_bar<PAIR>(ring_full(slot), static_cast<uint32_t>((seq / LY::kRing) & 1), abort_flag, p, 600 + slot)
+                 ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (lane != 0) {  // the phase is complete (the slot is not freed yet): acquire for this lane too
+        const uint32_t par = static_cast<uint32_t>((seq / LY::kRing) & 1);
+        (void)(PAIR ? mbar_try_wait_cluster(ring_full(slot), par) : mbar_try_wait(ring_full(slot), par));
+      }
+      int w[8];
+      ld_shared_8(ring_slot(slot), w);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_cluster(map_to_rank(ring_empty(slot), 0));
+        else mbar_arrive(ring_empty(slot));
+      }
+      if (!w[7]) break;
       Unit u;
-      if (!get_unit(p, cta, idx, u)) break;
+      unpack_unit(w, u);
       int tr, tq;
       unit_coords(p, u, tr, tq);
-      int ok = 1;
       if (lane == 0) ok = wait_bar(tfull_bar(acc), acc_phase, abort_flag, p, 400 + acc) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;

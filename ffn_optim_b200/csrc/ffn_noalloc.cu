@@ -148,7 +148,9 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   P.ldh = ldh;
   P.ldy = ldy;
   P.ws = ws;
-  P.counters = counters;
+  P.claims = reinterpret_cast<unsigned long long*>(counters);
+  P.counters = counters + ffnb200::kClaimWords;
+  P.dyn = plan.schedule == 2 ? 1 : 0;
   P.flags = flags;
   P.status = st;
   P.up = to_sched(plan.up);

@@ -90,14 +90,27 @@ def device_sm_count(device=None):
     return B200_SM_COUNT
 
 
+def problem_struct(problem, down_impl, gelu, block_num, sms, tile=None, raster_group=None, l2_policy=None,
+                   schedule=None):
+    """The C ABI's ffn_b200_problem for a validated Problem and the tuning overrides."""
+    from .. import _lib
+
+    return _lib.Problem(problem.m, problem.k, problem.h, problem.n, _lib.DTYPES[problem.dtype],
+                        _lib.DOWN_IMPL_CODES[down_impl], _lib.GELU_CODES[gelu], block_num, sms,
+                        _lib.TILE_VARIANTS[tile] if tile else 0, int(raster_group or 0),
+                        _lib.L2_POLICIES[l2_policy] if l2_policy else 0,
+                        _lib.SCHEDULES[schedule] if schedule else 0)
+
+
 def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational", sm_count=None, tile=None,
-              raster_group=None, l2_policy=None):
+              raster_group=None, l2_policy=None, schedule=None):
     """Plans one fused launch (reference ops/host/tiling.py:58-74).
 
     ``block_num`` None means one CTA per SM.  ``tile`` None picks the kernel variant
     automatically; a name of ``_lib.TILE_VARIANTS`` forces one (tests, benchmarks).
-    ``raster_group`` (tile rows per raster group) and ``l2_policy`` ('none' | 'stream_b')
-    override the automatic tuning.  Raises
+    ``raster_group`` (tile rows per raster group), ``l2_policy`` ('none' | 'stream_b' | ...)
+    and ``schedule`` ('static' | 'dynamic' data-parallel tile order) override the
+    automatic tuning.  Raises
     DependencyUnavailable for the full-load variants, NotApplicable for Stream-K without a
     tail wave (the reference's rule, applied to this kernel's tile grid), ValueError
     otherwise.
@@ -118,11 +131,10 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
         raise ValueError(f"l2_policy must be None or one of {sorted(_lib.L2_POLICIES)}")
     if raster_group is not None and (type(raster_group) is not int or raster_group < 1):
         raise ValueError("raster_group must be a positive integer")
+    if schedule is not None and schedule not in _lib.SCHEDULES:
+        raise ValueError(f"schedule must be None or one of {sorted(_lib.SCHEDULES)}")
     lib = _lib.load()
-    prob = _lib.Problem(problem.m, problem.k, problem.h, problem.n, _lib.DTYPES[problem.dtype],
-                        _lib.DOWN_IMPL_CODES[selection.down_impl], _lib.GELU_CODES[gelu], block_num, sms,
-                        _lib.TILE_VARIANTS[tile] if tile else 0, int(raster_group or 0),
-                        _lib.L2_POLICIES[l2_policy] if l2_policy else 0)
+    prob = problem_struct(problem, selection.down_impl, gelu, block_num, sms, tile, raster_group, l2_policy, schedule)
     info = _lib.PlanInfo()
     rc = lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info))
     if rc == _lib.ERR_NOT_APPLICABLE:
@@ -136,5 +148,5 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
     up = Tile(info.tile_m, info.tile_n, info.tile_k, info.stages)
     down = Tile(info.tile_m, info.tile_n, info.tile_k, info.stages)
     ws_shape = (2 * info.block_num * 128, info.tile_n)
-    kernel["overrides"] = {"tile": tile, "raster_group": raster_group, "l2_policy": l2_policy}
+    kernel["overrides"] = {"tile": tile, "raster_group": raster_group, "l2_policy": l2_policy, "schedule": schedule}
     return Plan(problem, selection, info.block_num, up, down, ws_shape, gelu, kernel)

@@ -174,7 +174,7 @@ class RowShardedFFN:
     no communication.  :meth:`run` returns this rank's rows of Y."""
 
     def __init__(self, x, w1, w2, *, group=None, down_impl="basic", block_num=None, gelu="rational",
-                 local=False, tile=None):
+                 local=False, tile=None, schedule=None):
         import torch.distributed as dist
 
         from .api import prepare_ffn
@@ -189,7 +189,8 @@ class RowShardedFFN:
         else:
             self.lo, self.hi = m_slices(m, self.world)[self.rank]
             x_local = x.reshape(m, k)[self.lo:self.hi]
-        self.prepared = prepare_ffn(x_local, w1, w2, down_impl=down_impl, block_num=block_num, gelu=gelu, tile=tile)
+        self.prepared = prepare_ffn(x_local, w1, w2, down_impl=down_impl, block_num=block_num, gelu=gelu, tile=tile,
+                                    schedule=schedule)
 
     def launches_per_run(self):
         return 1

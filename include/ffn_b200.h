@@ -72,7 +72,9 @@ typedef enum {
   FFN_B200_KERNEL_PIPE_TIMEOUT = 1, /* an on-chip pipeline wait ran past the wait limit */
   FFN_B200_KERNEL_DEP_TIMEOUT = 2,  /* a down tile waited too long for its hidden rows */
   FFN_B200_KERNEL_SK_TIMEOUT = 3,   /* a Stream-K owner waited too long for a partial */
-  FFN_B200_KERNEL_PEER_TIMEOUT = 4  /* a band owner waited too long for another GPU's partial */
+  FFN_B200_KERNEL_PEER_TIMEOUT = 4, /* a band owner waited too long for another GPU's partial */
+  FFN_B200_KERNEL_CLAIM_RANGE = 5   /* a tile claim fell outside this launch's range: the
+                                       counters were not reset after an earlier error */
 } ffn_b200_kernel_error;
 
 typedef struct {
@@ -91,6 +93,10 @@ typedef struct {
                            evict-first on the column operand (measured: far more DRAM traffic);
                            3: explicit evict-normal hint on every operand load;
                            4: evict-last on the row operand only */
+  int32_t schedule;     /* data-parallel tile order: 1 static (owner c takes tiles c, c+C, ...),
+                           2 dynamic (after its first tile each owner claims the next tile of the
+                           raster from a device counter); 0 = dynamic for CTA-pair tiles,
+                           static otherwise */
 } ffn_b200_problem;
 
 /* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
@@ -115,15 +121,17 @@ typedef struct {
   int64_t smem_bytes;
   ffn_b200_phase_plan up, down;
   int64_t workspace_floats; /* fp32 Stream-K partials: 2 phases x block_num x tile_m x tile_n */
-  int64_t counter_words;    /* u32 hidden-row-block readiness counters */
+  int64_t counter_words;    /* u32 words: two u64 tile-claim counters (up, down), then the
+                               hidden-row-block readiness counters */
   int64_t flag_words;       /* u32 Stream-K partial-ready flags: 2 x block_num */
   int64_t status_words;     /* i32 status words */
+  int32_t schedule;         /* resolved schedule: 1 static, 2 dynamic */
 } ffn_b200_plan;
 
 /* Device buffers.  ld* are row pitches in elements; each must be a multiple of 8 and each
  * base 16-byte aligned (TMA).  hidden is [M, ldh] scratch of the input dtype; y is the
  * [M, ldy] output.  workspace/counters/flags/status are sized by ffn_b200_plan and must be
- * zero-filled before the first run of a handle. */
+ * zero-filled before the first run of a handle; counters must be 8-byte aligned. */
 typedef struct {
   const void* x;  int64_t ldx;
   const void* w1; int64_t ldw1;
@@ -198,12 +206,26 @@ FFN_B200_EXPORT int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* handle,
 FFN_B200_EXPORT int ffn_b200_set_reduce_scatter(ffn_b200_handle* handle, int world, int rank, void* const* stage_ptrs,
                                                 void* const* flag_ptrs, void* y_local, int64_t ldy_local);
 
-/* Tracing: when `device_stamps` (a device uint64[block_num][8], or NULL to switch off) is
+/* Tracing: when `device_stamps` (a device uint64[block_num][16], or NULL to switch off) is
  * set, every later run writes per-CTA %globaltimer stamps (ns): 0 setup done, 1 first TMA
  * load, 2 first down tile's hidden rows ready, 3 last load, 4 last MMA commit, 5 last up
- * tile stored, 6 first down accumulator in the epilogue, 7 end.  Reference counterpart:
+ * tile stored, 6 first down accumulator in the epilogue, 7 end; word 8 holds the SM id the
+ * CTA ran on (words 9-15 are reserved).  Reference counterpart:
  * the separate profiler pass of performance/collect.py:38-72. */
 FFN_B200_EXPORT int ffn_b200_set_trace(ffn_b200_handle* handle, uint64_t* device_stamps);
+
+/* Work-list placement: `device_map` (a device int32[C], C = block_num / CTAs per tile, or
+ * NULL for launch order) gives the work-list index of each CTA (CTA pair); it must be a
+ * permutation of 0..C-1 and stay valid while set.  Tiles that share operand strips go to
+ * neighbouring indices, so the map decides which SMs (GPC, die) share them.  prepare sets
+ * one itself for CTA-pair plans that cover every SM: pairs numbered in the GPC-major order
+ * of a cooperative launch, measured once per device by two probe launches.  get_owner_map
+ * copies up to `capacity` entries of the map in use to host memory and sets `count` to C,
+ * or to 0 for launch order.  No reference counterpart (the reference's block-to-tile order
+ * is its launch order). */
+FFN_B200_EXPORT int ffn_b200_set_owner_map(ffn_b200_handle* handle, const int32_t* device_map);
+FFN_B200_EXPORT int ffn_b200_get_owner_map(const ffn_b200_handle* handle, int32_t* host_out, int32_t capacity,
+                                           int32_t* count);
 
 FFN_B200_EXPORT int ffn_b200_get_plan(const ffn_b200_handle* handle, ffn_b200_plan* plan);
 FFN_B200_EXPORT int ffn_b200_destroy(ffn_b200_handle* handle);

@@ -32,3 +32,32 @@ def test_dependency_wait_times_out_and_recovers(case_id):
     assert torch.equal(y, good)
     torch.cuda.synchronize()
     assert np.isfinite(y.float().cpu().numpy()).all()
+
+
+def test_dynamic_claims_without_reset_report_and_recover():
+    """A launch that aborted leaves the tile-claim counter short of its epoch base; a next
+    launch without the reset rejects its out-of-range claims (status 5, or a timeout in the
+    CTAs that wait behind them) instead of using them as tile coordinates, and a reset
+    restores correct results."""
+    m, k, h, n = 8192, 512, 2048, 1024
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(m, k, generator=g).bfloat16().cuda()
+    w1 = (torch.randn(h, k, generator=g) * k ** -0.5).bfloat16().cuda()
+    w2 = (torch.randn(n, h, generator=g) * h ** -0.5).bfloat16().cuda()
+    prepared = prepare_ffn(x, w1, w2, schedule="dynamic")
+    good = prepared.run().clone()
+    prepared.check()
+    prepared.set_wait_limit(0.2)
+    prepared.set_fault_injection(1)
+    prepared.run()
+    torch.cuda.synchronize()
+    assert prepared.status()[0] == 2
+    prepared.set_fault_injection(0)
+    prepared.run()  # no reset in between
+    torch.cuda.synchronize()
+    assert prepared.status()[0] != 0
+    prepared.reset()
+    prepared.set_wait_limit(2.0)
+    y = prepared.run()
+    prepared.check()
+    assert torch.equal(y, good)

@@ -141,6 +141,57 @@ def test_full_size_vs_golden_and_oracle(case_id, tile):
     assert np.array_equal(bits_of(y), first), "run-to-run results differ"
 
 
+def test_pair_placement_map_keeps_results():
+    """CTA-pair plans get a measured owner map (a permutation of the pairs); placing the
+    tiles in launch order instead, or in a reversed order, gives bit-identical output."""
+    m, k, h, n = 4096, 1024, 2048, 512
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(m, k, generator=g).bfloat16().cuda()
+    w1 = (torch.randn(h, k, generator=g) * k ** -0.5).bfloat16().cuda()
+    w2 = (torch.randn(n, h, generator=g) * h ** -0.5).bfloat16().cuda()
+    prepared, y = run(x, w1, w2, tile="pair256x256")
+    owners = prepared.owner_map()
+    pairs = prepared.plan.block_num // 2
+    if prepared.plan.block_num == torch.cuda.get_device_properties(0).multi_processor_count:
+        assert owners is not None and sorted(owners) == list(range(pairs))
+    first = bits_of(y)
+    for order in (None, list(range(pairs))[::-1]):
+        prepared.set_owner_map(order)
+        assert prepared.owner_map() == order
+        prepared.run()
+        prepared.check()
+        assert np.array_equal(bits_of(y), first)
+    with pytest.raises(ValueError):
+        prepared.set_owner_map([0] * pairs)
+    smid = prepared.trace()["smid"]
+    assert len(set(smid)) == prepared.plan.block_num
+
+
+@pytest.mark.parametrize("tile", ["cta128x256", "pair256x256", "cta128x128"])
+def test_static_and_dynamic_schedules_agree(tile):
+    """Every data-parallel tile is computed whole by one CTA and Stream-K parts keep their
+    static split, so the tile order (static or claimed) cannot change a single bit;
+    repeated dynamic launches (epoch bases) agree too."""
+    m, k, h, n = 12288, 1024, 4096, 1536
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(m, k, generator=g).bfloat16().cuda()
+    w1 = (torch.randn(h, k, generator=g) * k ** -0.5).bfloat16().cuda()
+    w2 = (torch.randn(n, h, generator=g) * h ** -0.5).bfloat16().cuda()
+    outs = []
+    for schedule in ("static", "dynamic"):
+        for down in ("basic", "streamk"):
+            prepared, y = run(x, w1, w2, tile=tile, schedule=schedule, down_impl=down)
+            assert prepared.plan.kernel["schedule"] == {"static": 1, "dynamic": 2}[schedule]
+            first = bits_of(y)
+            for _ in range(3):
+                prepared.run()
+            prepared.check()
+            assert np.array_equal(bits_of(y), first)
+            outs.append(first)
+    assert all(np.array_equal(o, outs[0]) for o in outs[1:]) or all(
+        np.array_equal(outs[i], outs[i + 2]) for i in (0, 1))
+
+
 RAGGED = [
     # (M, K, H, N, dtype)
     (1, 8, 8, 8, torch.bfloat16),

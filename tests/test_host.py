@@ -166,6 +166,46 @@ def test_plan_covers_every_k_block_once(case_id, tile):
             assert k["down"]["sk_tiles"] == 0
 
 
+def _claim_model(dp, C, epochs, rng):
+    """Python model of the device's dynamic schedule (producer loop of the fused kernel):
+    owner c takes tile c first, then claims tile C + (counter - base) until a claim lands at
+    or past dp.  Owners run in a random interleaving; returns the tiles per launch and the
+    counter."""
+    span = max(dp - C, 0) + C
+    counter = 0
+    launches = []
+    for epoch in range(1, epochs + 1):
+        base = (epoch - 1) * span
+        t_end = max(dp, C) + C
+        state = {c: (c, False) for c in range(C)}  # next tile, came from a claim
+        done = []
+        active = list(range(C))
+        while active:
+            c = active[rng.integers(len(active))]
+            t, claimed = state[c]
+            if t >= dp and not claimed:          # no static first tile: one claim
+                t, claimed = C + counter - base, True
+                counter += 1
+            assert not claimed or C <= t < t_end
+            if t >= dp:
+                active.remove(c)
+                continue
+            done.append(t)
+            state[c] = (C + counter - base, True)
+            counter += 1
+        launches.append(done)
+        assert counter == epoch * span
+    return launches, counter
+
+
+@pytest.mark.parametrize("dp,C", [(0, 4), (3, 8), (8, 8), (9, 8), (1000, 148), (28672, 148), (7, 74)])
+def test_dynamic_claims_cover_every_tile_once(dp, C):
+    rng = np.random.Generator(np.random.PCG64(dp * 7 + C))
+    launches, _ = _claim_model(dp, C, 3, rng)
+    for done in launches:
+        assert sorted(done) == list(range(dp))
+
+
 def test_baseline_variants():
     want = {"cfg3_bf16": (1, 16), "cfg4_bf16": (0, 256), "cfg5_bf16": (0, 256), "cfg1_fp16": (0, 128),
             "cfg2_bf16": (0, 128)}
