@@ -47,6 +47,8 @@ def parse():
                          "fused into the kernel (NVLink peer stores), m = M-sharded")
     ap.add_argument("--chunks", type=int, default=4)
     ap.add_argument("--tile", default=None, help="force a kernel variant (see ffn_optim_b200._lib.TILE_VARIANTS)")
+    ap.add_argument("--down-impl", choices=("basic", "streamk", "full_load_a"), default=None,
+                    help="override the workload's down_impl")
     ap.add_argument("--schedule", choices=("static", "dynamic"), default=None,
                     help="data-parallel tile order (default: dynamic for CTA-pair tiles, static otherwise)")
     ap.add_argument("--cpu-rows", type=int, default=1024)
@@ -272,7 +274,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     case = C.get_case(args.workload)
     p, x, w1, w2 = device_inputs(case, dev)
-    down = case.get("down_impl", "basic")
+    down = args.down_impl or case.get("down_impl", "basic")
 
     if world == 1:
         runner = prepare_ffn(x, w1, w2, down_impl=down, tile=args.tile, schedule=args.schedule)

@@ -30,7 +30,7 @@ DOWN_IMPL_CODES = {"basic": 0, "full_load_a": 1, "full_load_b": 2, "streamk": 3}
 GELU_CODES = {"rational": 0, "erf": 1}
 # Kernel variants selectable through prepare_ffn(..., tile=...) (None = automatic).
 TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5,
-                 "swap16k4": 6, "swap64k2": 7}
+                 "swap16k4": 6, "swap64k2": 7, "rowblock64": 8, "rowblock128": 9, "rowblock256": 10}
 L2_POLICIES = {"none": 1, "stream_b": 2, "normal": 3, "keep_a": 4}
 SCHEDULES = {"static": 1, "dynamic": 2}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",

@@ -19,6 +19,7 @@
 
 #include "../../include/ffn_b200.h"
 #include "ffn_kernel.cuh"
+#include "ffn_rowblock.cuh"
 
 namespace ffnb200 {
 const int32_t* internal_pair_owner_map(int device, int grid, int smem);  // ffn_placement.cu
@@ -33,17 +34,21 @@ using KernelFn = void (*)(const Params);
 struct Variant {
   int bn, stages;
   bool swap, pair;
-  int ksub;  // 64-wide K sub-blocks per pipeline stage
-  int epi;   // epilogue warps (4, or 8 = two per TMEM sub-partition for short tiles)
+  int ksub;       // 64-wide K sub-blocks per pipeline stage
+  int epi;        // epilogue warps (4, or 8 = two per TMEM sub-partition for short tiles)
+  bool rowblock;  // hidden-resident row-block kernel (down_impl full_load_a); bn = Y width
 };
 // 0: prefill tiles 128x256 (one CTA), 1: 128x128 for small grids, 2/3: swap-AB decode
 // tiles (16 / 64 tokens), 4: prefill tiles 256x256 computed by a CTA pair (cta_group::2),
-// 5/6: swap-AB decode tiles with 256/128-wide K stages (longer contiguous weight reads).
-constexpr Variant kVariants[] = {{256, 4, false, false, 1, 4}, {128, 4, false, false, 1, 8},
-                                 {16, 8, true, false, 1, 8},   {64, 8, true, false, 1, 8},
-                                 {256, 6, false, true, 1, 4},  {16, 3, true, false, 4, 8},
-                                 {64, 4, true, false, 2, 8}};
-constexpr int kNumVariants = 7;
+// 5/6: swap-AB decode tiles with 256/128-wide K stages (longer contiguous weight reads),
+// 7/8/9: hidden-resident row blocks with a 64/128/256-column Y accumulator.
+constexpr Variant kVariants[] = {{256, 4, false, false, 1, 4, false}, {128, 4, false, false, 1, 8, false},
+                                 {16, 8, true, false, 1, 8, false},   {64, 8, true, false, 1, 8, false},
+                                 {256, 6, false, true, 1, 4, false},  {16, 3, true, false, 4, 8, false},
+                                 {64, 4, true, false, 2, 8, false},   {64, 4, false, false, 1, 8, true},
+                                 {128, 4, false, false, 1, 8, true},  {256, 4, false, false, 1, 8, true}};
+constexpr int kNumVariants = 10;
+constexpr int kFirstRowblock = 7;
 
 template <int BN, int ST, bool SW, bool PR, int KS, int EP>
 KernelFn pick_kernel(int bf16, int gelu) {
@@ -60,12 +65,21 @@ KernelFn pick_kernel(int bf16, int gelu) {
   X(4, 256, 6, false, true, 1, 4)             \
   X(5, 16, 3, true, false, 4, 8)              \
   X(6, 64, 4, true, false, 2, 8)
+template <int NY>
+KernelFn pick_rowblock(int bf16, int gelu) {
+  using namespace ffnb200;
+  if (bf16) return gelu ? ffn_rowblock_kernel<NY, 4, true, 1> : ffn_rowblock_kernel<NY, 4, true, 0>;
+  return gelu ? ffn_rowblock_kernel<NY, 4, false, 1> : ffn_rowblock_kernel<NY, 4, false, 0>;
+}
 KernelFn kernel_for(int variant, int bf16, int gelu) {
   switch (variant) {
 #define X(id, bn, st, sw, pr, ks, ep) \
   case id: return pick_kernel<bn, st, sw, pr, ks, ep>(bf16, gelu);
     FFN_B200_VARIANTS(X)
 #undef X
+    case 7: return pick_rowblock<64>(bf16, gelu);
+    case 8: return pick_rowblock<128>(bf16, gelu);
+    case 9: return pick_rowblock<256>(bf16, gelu);
   }
   return nullptr;
 }
@@ -75,11 +89,15 @@ int smem_for(int variant) {
   case id: return ffnb200::Layout<bn, st, sw, pr, ks, ep>::kSmem;
     FFN_B200_VARIANTS(X)
 #undef X
+    case 7: return ffnb200::RowLayout<64, 4>::kSmem;
+    case 8: return ffnb200::RowLayout<128, 4>::kSmem;
+    case 9: return ffnb200::RowLayout<256, 4>::kSmem;
   }
   return 0;
 }
 int threads_for(int variant) { return ffnb200::kCtrlThreads + 32 * kVariants[variant].epi; }
 int tmem_cols_for(int variant) {
+  if (kVariants[variant].rowblock) return 512;
   const int c = 2 * kVariants[variant].bn;
   return c < 32 ? 32 : c;
 }
@@ -127,6 +145,49 @@ int phase_plan(const PhaseInput& in, int tile_m, int bn, int tile_k, int C, bool
     out->sk_iters = 0;
     out->sk_rem = 0;
   }
+  return FFN_B200_OK;
+}
+
+// down_impl full_load_a: hidden-resident row blocks (ffn_rowblock.cuh).  One CTA per row
+// block of 128 tokens, up to `grid` CTAs; the Y row block lives in TMEM next to the two up
+// accumulators, so it applies when N <= 256 (as the reference's full-load tiling applies
+// only when the operand fits on chip).
+int plan_rowblock(const ffn_b200_problem& pr, int grid, ffn_b200_plan* out) {
+  if (pr.n > 256) return FFN_B200_ERR_NOT_APPLICABLE;
+  int variant = pr.n <= 64 ? kFirstRowblock : (pr.n <= 128 ? kFirstRowblock + 1 : kFirstRowblock + 2);
+  if (pr.tile_variant > 0) {
+    const int forced = pr.tile_variant - 1;
+    if (!kVariants[forced].rowblock || kVariants[forced].bn < pr.n) return FFN_B200_ERR_INVALID;
+    variant = forced;
+  }
+  const Variant& v = kVariants[variant];
+  const int64_t rows = cdiv(pr.m, ffnb200::kBM);
+  const int64_t chunks = cdiv(pr.h, 128);
+  if (rows * chunks >= (int64_t(1) << 31)) return FFN_B200_ERR_TOO_LARGE;
+  const int C = static_cast<int>(rows < grid ? rows : grid);
+  auto fill = [&](ffn_b200_phase_plan* ph, int64_t tq, int64_t depth) {
+    ph->tiles_r = static_cast<int32_t>(rows);
+    ph->tiles_q = static_cast<int32_t>(tq);
+    ph->tiles = static_cast<int32_t>(rows * tq);
+    ph->k_blocks = static_cast<int32_t>(cdiv(depth, ffnb200::kBK));
+    ph->dp_tiles = ph->tiles;
+    ph->group = 1;
+  };
+  fill(&out->up, chunks, pr.k);
+  fill(&out->down, 1, pr.h);
+  out->variant = variant;
+  out->tile_m = ffnb200::kBM;
+  out->tile_n = v.bn;
+  out->tile_k = ffnb200::kBK;
+  out->stages = v.stages;
+  out->block_num = C;
+  out->tmem_cols = tmem_cols_for(variant);
+  out->smem_bytes = smem_for(variant);
+  out->workspace_floats = 4;
+  out->counter_words = ffnb200::kClaimWords + 2;
+  out->flag_words = 2;
+  out->status_words = 4;
+  out->schedule = 1;
   return FFN_B200_OK;
 }
 
@@ -222,8 +283,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   if (pr->dtype != FFN_B200_F16 && pr->dtype != FFN_B200_BF16) return FFN_B200_ERR_INVALID;
   if (pr->gelu != FFN_B200_GELU_RATIONAL && pr->gelu != FFN_B200_GELU_ERF) return FFN_B200_ERR_INVALID;
   if (pr->down_impl < 0 || pr->down_impl > 3) return FFN_B200_ERR_INVALID;
-  if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_A || pr->down_impl == FFN_B200_DOWN_FULL_LOAD_B)
-    return FFN_B200_ERR_UNAVAILABLE;
+  if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_B) return FFN_B200_ERR_UNAVAILABLE;
   int sm = pr->sm_count;
   if (sm <= 0) {
     const int rc = query_sm_count(&sm);
@@ -236,6 +296,8 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   if (pr->schedule < 0 || pr->schedule > 2) return FFN_B200_ERR_INVALID;
 
   std::memset(out, 0, sizeof(*out));
+  if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_A) return plan_rowblock(*pr, grid, out);
+  if (pr->tile_variant > 0 && kVariants[pr->tile_variant - 1].rowblock) return FFN_B200_ERR_INVALID;
   int variant;
   if (pr->tile_variant > 0) {
     variant = pr->tile_variant - 1;
@@ -332,18 +394,20 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   if (rc) return rc;
   if (plan.block_num > sm) return FFN_B200_ERR_DEVICE;
 
-  // Buffers: TMA needs 16-byte aligned bases and pitches.
-  const void* bases[] = {b->x, b->w1, b->w2, b->hidden, b->y, b->workspace};
+  // Buffers: TMA needs 16-byte aligned bases and pitches.  The row-block kernel keeps the
+  // hidden activations on chip and ignores `hidden` / `ldh`.
+  const bool rowblock = kVariants[plan.variant].rowblock;
+  const void* bases[] = {b->x, b->w1, b->w2, b->y, b->workspace, rowblock ? b->y : b->hidden};
   for (const void* p : bases)
     if (!p) return FFN_B200_ERR_INVALID;
   for (const void* p : bases)
     if (!aligned16(p)) return FFN_B200_ERR_ALIGNMENT;
   if (!b->counters || !b->flags || !b->status) return FFN_B200_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(b->counters) & 7u) return FFN_B200_ERR_ALIGNMENT;
-  const int64_t pitches[] = {b->ldx, b->ldw1, b->ldw2, b->ldh, b->ldy};
+  const int64_t pitches[] = {b->ldx, b->ldw1, b->ldw2, rowblock ? b->ldy : b->ldh, b->ldy};
   for (int64_t p : pitches)
     if (p <= 0 || (p % 8) != 0) return FFN_B200_ERR_ALIGNMENT;
-  if (b->ldx < prob.k || b->ldw1 < prob.k || b->ldw2 < prob.h || b->ldh < prob.h || b->ldy < prob.n)
+  if (b->ldx < prob.k || b->ldw1 < prob.k || b->ldw2 < prob.h || (!rowblock && b->ldh < prob.h) || b->ldy < prob.n)
     return FFN_B200_ERR_INVALID;
 
   rc = get_encode();
@@ -366,7 +430,13 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   const bool sw = plan.swap_ab != 0;
   // Up:   normal A = X [M,K] (128-row boxes), B = W1 [H,K] (bn-row boxes); swap exchanges them.
   // Down: normal A = hidden [M,H], B = W2 [N,H]; swap exchanges them.
-  if (!sw) {
+  if (rowblock) {
+    // X [M,K] and W1 [H,K] in 128-row boxes, W2 [N,H] in one box of tile_n rows, Y stores.
+    rc = encode_2d(&P.tm_a_up, b->x, dt, prob.k, prob.m, b->ldx, 64, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_up, b->w1, dt, prob.k, prob.h, b->ldw1, 64, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_dn, b->w2, dt, prob.h, prob.n, b->ldw2, 64, static_cast<uint32_t>(plan.tile_n));
+    if (!rc) rc = encode_2d(&P.tm_st_y, b->y, dt, prob.n, prob.m, b->ldy, 64, ffnb200::kStoreRows);
+  } else if (!sw) {
     rc = encode_2d(&P.tm_a_up, b->x, dt, prob.k, prob.m, b->ldx, 64, 128);
     if (!rc) rc = encode_2d(&P.tm_b_up, b->w1, dt, prob.k, prob.h, b->ldw1, 64, bn);
     if (!rc) rc = encode_2d(&P.tm_a_dn, b->hidden, dt, prob.h, prob.m, b->ldh, 64, 128);
@@ -509,7 +579,8 @@ int ffn_b200_run(ffn_b200_handle* h, void* stream) {
     attr[0].val.cooperative = 1;
   }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  // Row-block plans have no waits between CTAs: a plain launch, no co-residency needed.
+  cfg.numAttrs = kVariants[h->plan.variant].rowblock ? 0 : 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, h->kernel, h->params);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -695,6 +766,7 @@ int ffn_b200_launch(const ffn_b200_problem* pr, const ffn_b200_buffers* b, void*
 
 // Internal accessors used by the allocation-free entry point in ffn_noalloc.cu; not exported.
 namespace ffnb200 {
+bool internal_is_rowblock(int variant) { return variant >= 0 && variant < kNumVariants && kVariants[variant].rowblock; }
 void (*internal_kernel_for(int variant, int bf16, int gelu))(const Params) {
   return kernel_for(variant, bf16, gelu);
 }

@@ -34,6 +34,7 @@ void (*internal_kernel_for(int variant, int bf16, int gelu))(const Params);
 int internal_encode_2d(CUtensorMap* tm, const void* base, int dtype, int64_t inner, int64_t outer, int64_t pitch,
                        uint32_t box_inner, uint32_t box_outer);
 int internal_threads_for(int variant);
+bool internal_is_rowblock(int variant);
 }  // namespace ffnb200
 
 // The scratch.  In host code this name is only a stand-in for the symbol; the device address
@@ -101,8 +102,10 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   }
 
   // Scratch layout: hidden [M, ldh] | fp32 partials | counters | flags | status, 256-B aligned.
+  // The row-block kernel (full_load_a) keeps hidden on chip and needs no hidden scratch.
+  const bool rowblock = internal_is_rowblock(plan.variant);
   const int64_t ldh = round_up(prob.h, 8);
-  const int64_t off_ws = round_up(prob.m * ldh * 2, 256);
+  const int64_t off_ws = rowblock ? 0 : round_up(prob.m * ldh * 2, 256);
   const int64_t off_cnt = off_ws + round_up(plan.workspace_floats * 4, 256);
   const int64_t off_flg = off_cnt + round_up(plan.counter_words * 4, 256);
   const int64_t off_st = off_flg + round_up(plan.flag_words * 4, 256);
@@ -122,7 +125,12 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   std::memset(&P, 0, sizeof(P));
   const int dt = prob.dtype;
   const uint32_t bn = static_cast<uint32_t>(plan.tile_n);
-  if (!plan.swap_ab) {
+  if (rowblock) {
+    rc = internal_encode_2d(&P.tm_a_up, x, dt, prob.k, prob.m, ldx, 64, 128);
+    if (!rc) rc = internal_encode_2d(&P.tm_b_up, w1, dt, prob.k, prob.h, ldw1, 64, 128);
+    if (!rc) rc = internal_encode_2d(&P.tm_b_dn, w2, dt, prob.h, prob.n, ldw2, 64, bn);
+    if (!rc) rc = internal_encode_2d(&P.tm_st_y, y, dt, prob.n, prob.m, ldy, 64, kStoreRows);
+  } else if (!plan.swap_ab) {
     rc = internal_encode_2d(&P.tm_a_up, x, dt, prob.k, prob.m, ldx, 64, 128);
     if (!rc) rc = internal_encode_2d(&P.tm_b_up, w1, dt, prob.k, prob.h, ldw1, 64, bn);
     if (!rc) rc = internal_encode_2d(&P.tm_a_dn, hidden, dt, prob.h, prob.m, ldh, 64, 128);

@@ -1,0 +1,340 @@
+// Row-block FFN with the hidden activations resident on chip: the B200 form of the
+// reference's down_impl "full_load_a" (the down GEMM's A operand -- the hidden row block --
+// fully loaded on chip instead of streamed from global memory; ops/host/dispatch.py:15,
+// spec/v1_spec.md:156).
+//
+// One CTA owns 128 tokens (a row block) at a time and walks H in chunks of 128 columns:
+//
+//   up(j):   D_up[j%2]  = X[rb, :] . W1[128j : 128j+128, :]^T      (TMEM, fp32, 128 cols)
+//   epi(j):  hid[j%2]   = RN(GELU(D_up[j%2]))                       (shared memory, 128B-swizzled
+//                                                                    K-major: the A operand)
+//   down(j): D_y       += hid[j%2] . W2[:, 128j : 128j+128]^T       (TMEM, fp32, NY cols)
+//
+// and after the last chunk stores D_y as Y[rb, :N].  The MMA issuer runs up(j+1) while the
+// epilogue converts chunk j, so the tensor core alternates up and down chunks:
+// up(0) up(1) down(0) up(2) down(1) ... down(J-1).  Hidden never reaches global memory and
+// no CTA waits on another, so the launch needs no co-residency.  TMEM holds both up
+// accumulators (256 columns) and the Y accumulator (NY <= 256 columns): the variant
+// applies when N <= 256.
+//
+// Arithmetic is that of the two-phase kernel: fp32 accumulation over K, GELU of the fp32
+// sum, hidden rounded once to the input dtype, fp32 accumulation over H, one rounding of
+// Y.  Only the order of the H summation differs (chunks of 128 in ascending order, inside
+// one accumulator).
+#pragma once
+
+#include "ffn_kernel.cuh"
+
+namespace ffnb200 {
+
+template <int NY, int STAGES>
+struct RowLayout {
+  static constexpr int kEpiWarps = 8;                   // two per TMEM sub-partition
+  static constexpr int kThreads = kCtrlThreads + 32 * kEpiWarps;
+  static constexpr int kChunk = 128;                    // H columns per up chunk
+  static constexpr int kStage = 32768;                  // X + W1 k-block, or one W2 k-block
+  static constexpr int kHidBuf = kChunk * kBM * 2;      // one hidden chunk: 2 k-blocks of 16 KB
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmem = 1024 + STAGES * kStage + 2 * kHidBuf + kBarBytes;
+  static constexpr int kTmemCols = 512;                 // up accumulators 0..255, Y 256..256+NY
+  static_assert(NY == 64 || NY == 128 || NY == 256, "Y accumulator width");
+  static_assert(NY * kBK * 2 <= kStage, "W2 k-block fits a stage");
+  static_assert((2 * STAGES + 11) * 8 + 8 <= kBarBytes, "barrier area");
+  static_assert(kSmem <= 232448, "dynamic shared memory per CTA");
+};
+
+template <int NY, int STAGES, bool BF16, int GELU>
+__global__ void __launch_bounds__(kCtrlThreads + 32 * 8, 1) ffn_rowblock_kernel(const __grid_constant__ Params p) {
+  using LY = RowLayout<NY, STAGES>;
+  constexpr uint32_t kIdescUp = make_idesc<BF16, LY::kChunk, kBM>();
+  constexpr uint32_t kIdescDn = make_idesc<BF16, NY, kBM>();
+  constexpr uint32_t kUpBytes = 2 * kABytes;           // X k-block + W1 k-block (128 rows each)
+  constexpr uint32_t kDnBytes = NY * kBK * 2;          // W2 k-block
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sS = base;                             // operand ring
+  const uint32_t sH = sS + STAGES * LY::kStage;         // two hidden chunk buffers
+  const uint32_t sBar = sH + 2 * LY::kHidBuf;
+  auto full_bar = [&](int s) { return sBar + 8u * s; };
+  auto empty_bar = [&](int s) { return sBar + 8u * (STAGES + s); };
+  auto ufull = [&](int a) { return sBar + 8u * (2 * STAGES + a); };
+  auto uempty = [&](int a) { return sBar + 8u * (2 * STAGES + 2 + a); };
+  auto hfull = [&](int b) { return sBar + 8u * (2 * STAGES + 4 + b); };
+  auto hempty = [&](int b) { return sBar + 8u * (2 * STAGES + 6 + b); };
+  const uint32_t yfull = sBar + 8u * (2 * STAGES + 8);
+  const uint32_t yempty = sBar + 8u * (2 * STAGES + 9);
+  const uint32_t drain_bar = sBar + 8u * (2 * STAGES + 10);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (sBar - base) + 8 * (2 * STAGES + 11));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int RB = p.up.tiles_r;   // row blocks
+  const int J = p.up.tiles_q;    // H chunks
+  const int KB = p.up.L;         // 64-wide k-blocks of K
+
+  if (threadIdx.x == 0) {
+#pragma unroll 1
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(ufull(a), 1);
+      mbar_init(uempty(a), LY::kEpiWarps);
+      mbar_init(hfull(a), LY::kEpiWarps);
+      mbar_init(hempty(a), 1);
+    }
+    mbar_init(yfull, 1);
+    mbar_init(yempty, LY::kEpiWarps);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_async_shared();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tm_a_up);
+    prefetch_tmap(&p.tm_b_up);
+    prefetch_tmap(&p.tm_b_dn);
+    prefetch_tmap(&p.tm_st_y);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), LY::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) trace_mark(p, kTrStart);
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      auto next_stage = [&]() -> bool {
+        if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) return false;
+        return true;
+      };
+      auto advance = [&]() {
+        ++issued;
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      };
+#pragma unroll 1
+      for (int rb = blockIdx.x; rb < RB && ok; rb += gridDim.x) {
+#pragma unroll 1
+        for (int j = 0; j <= J && ok; ++j) {
+          if (j < J) {  // up(j): X and W1 k-blocks
+#pragma unroll 1
+            for (int kb = 0; kb < KB; ++kb) {
+              if (!next_stage()) { ok = false; break; }
+              const uint32_t st = sS + stage * LY::kStage;
+              mbar_expect_tx(full_bar(stage), kUpBytes);
+              tma_load_2d(st, &p.tm_a_up, kb * kBK, rb * kBM, full_bar(stage));
+              tma_load_2d(st + kABytes, &p.tm_b_up, kb * kBK, j * LY::kChunk, full_bar(stage));
+              if (issued == 0) trace_mark(p, kTrFirstLoad);
+              advance();
+            }
+          }
+          if (ok && j >= 1) {  // down(j-1): the two W2 k-blocks of chunk j-1
+#pragma unroll 1
+            for (int kk = 0; kk < 2; ++kk) {
+              if (!next_stage()) { ok = false; break; }
+              mbar_expect_tx(full_bar(stage), kDnBytes);
+              tma_load_2d(sS + stage * LY::kStage, &p.tm_b_dn, ((j - 1) * 2 + kk) * kBK, 0, full_bar(stage));
+              advance();
+            }
+          }
+        }
+      }
+      trace_mark(p, kTrLastLoad);
+      // Every issued load lands before the CTA may exit (one deadline for the drain).
+      const long long first = issued > STAGES ? issued - STAGES : 0;
+      const uint64_t t0 = gtimer();
+      bool late = false;
+#pragma unroll 1
+      for (long long i = first; i < issued && !late; ++i) {
+        const int s = static_cast<int>(i % STAGES);
+        const uint32_t par = static_cast<uint32_t>((i / STAGES) & 1);
+        while (!mbar_try_wait(full_bar(s), par)) {
+          if (gtimer() - t0 > p.wait_limit_ns) { late = true; break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int ucnt = 0, dcnt = 0, rcnt = 0;
+      bool ok = true;
+      auto up_chunk = [&]() -> bool {
+        const int a = ucnt & 1;
+        if (!wait_bar(uempty(a), ((ucnt >> 1) & 1) ^ 1u, abort_flag, p, 200 + a)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(a * LY::kChunk);
+#pragma unroll 1
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!wait_bar(full_bar(stage), phase, abort_flag, p, 300 + stage)) return false;
+          tc_fence_after();
+          const uint32_t st = sS + stage * LY::kStage;
+          const uint64_t da = sw128_desc(st);
+          const uint64_t db = sw128_desc(st + kABytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16(d, da + 2 * k, db + 2 * k, kIdescUp, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        umma_commit(ufull(a));
+        ++ucnt;
+        return true;
+      };
+      auto down_chunk = [&](bool first) -> bool {
+        const int b = dcnt & 1;
+        if (!wait_bar(hfull(b), (dcnt >> 1) & 1, abort_flag, p, 220 + b)) return false;
+        if (first && !wait_bar(yempty, (rcnt & 1) ^ 1u, abort_flag, p, 240)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem_base + 256u;
+#pragma unroll 1
+        for (int kk = 0; kk < 2; ++kk) {
+          if (!wait_bar(full_bar(stage), phase, abort_flag, p, 300 + stage)) return false;
+          tc_fence_after();
+          const uint64_t da = sw128_desc(sH + b * LY::kHidBuf + kk * kABytes);
+          const uint64_t db = sw128_desc(sS + stage * LY::kStage);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16(d, da + 2 * k, db + 2 * k, kIdescDn, (!first || kk > 0 || k > 0) ? 1u : 0u);
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        umma_commit(hempty(b));
+        ++dcnt;
+        return true;
+      };
+#pragma unroll 1
+      for (int rb = blockIdx.x; rb < RB && ok; rb += gridDim.x) {
+#pragma unroll 1
+        for (int j = 0; j <= J && ok; ++j) {
+          if (j < J && !up_chunk()) ok = false;
+          if (ok && j >= 1 && !down_chunk(j == 1)) ok = false;
+        }
+        if (!ok) break;
+        umma_commit(yfull);
+        ++rcnt;
+      }
+      trace_mark(p, kTrLastMma);
+      umma_commit(drain_bar);
+      const uint64_t t0 = gtimer();
+      while (!mbar_try_wait(drain_bar, 0)) {
+        if (gtimer() - t0 > p.wait_limit_ns) break;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..9)
+    const int ew = warp - kCtrlThreads / 32;  // 0..7
+    const int sub = warp & 3;           // TMEM lane sub-partition this warp may access
+    const int part = ew >> 2;           // which 64-column half of a chunk
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    // This warp's 4 KB region in hidden buffer b: k-block `part`, rows sub*32.. (32 x 128 B).
+    auto region = [&](int b) { return sH + static_cast<uint32_t>(b * LY::kHidBuf + part * kABytes + sub * 32 * 128); };
+    int ucnt = 0, hcnt = 0, rcnt = 0;
+    bool stores_pending = false;
+    int ok = 1;
+    auto warp_wait = [&](uint32_t bar, uint32_t par, int aux) {
+      int r = 1;
+      if (lane == 0) r = wait_bar(bar, par, abort_flag, p, aux) ? 1 : 0;
+      return __shfl_sync(0xffffffffu, r, 0);
+    };
+    auto store_swizzled = [&](uint32_t reg, const uint32_t* pk) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t addr = reg + lane * 128 + ((c ^ (lane & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
+                     "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+                     : "memory");
+      }
+    };
+#pragma unroll 1
+    for (int rb = blockIdx.x; rb < RB && ok; rb += gridDim.x) {
+#pragma unroll 1
+      for (int j = 0; j < J && ok; ++j) {
+        const int a = ucnt & 1;
+        ok = warp_wait(ufull(a), (ucnt >> 1) & 1, 400 + a);
+        if (!ok) break;
+        tc_fence_after();
+        float v[64];
+        const uint32_t t = tmem_base + lane_off + static_cast<uint32_t>(a * LY::kChunk + part * 64);
+        tmem_ld32(t, v);
+        tmem_ld32(t + 32, v + 32);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(uempty(a));
+        ++ucnt;
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = pack2<BF16>(gelu<GELU>(v[2 * i]), gelu<GELU>(v[2 * i + 1]));
+        const int b = hcnt & 1;
+        ok = warp_wait(hempty(b), ((hcnt >> 1) & 1) ^ 1u, 420 + b);
+        if (!ok) break;
+        if (stores_pending) {  // Y stores of the previous row block read this region
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          stores_pending = false;
+        }
+        store_swizzled(region(b), pk);
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(hfull(b));
+        ++hcnt;
+      }
+      if (!ok) break;
+      // Y of the row block: 64-column chunks split over the two warps of a sub-partition,
+      // staged in this warp's own regions of the (now idle) hidden buffers.
+      ok = warp_wait(yfull, rcnt & 1, 440);
+      if (!ok) break;
+      tc_fence_after();
+      int used = 0;
+#pragma unroll 1
+      for (int yc = part; yc < NY / 64 && yc * 64 < p.N; yc += 2) {
+        float v[64];
+        const uint32_t t = tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64);
+        tmem_ld32(t, v);
+        tmem_ld32(t + 32, v + 32);
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
+        const uint32_t reg = region(used);
+        store_swizzled(reg, pk);
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&p.tm_st_y, reg, yc * 64, rb * kBM + sub * 32);
+          bulk_commit();
+        }
+        ++used;
+      }
+      stores_pending = used > 0;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(yempty);
+      ++rcnt;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) trace_mark(p, kTrEnd);
+  if (warp == 1) tmem_dealloc(tmem_base, LY::kTmemCols);
+}
+
+}  // namespace ffnb200

@@ -10,7 +10,8 @@ from dataclasses import dataclass
 
 DOWN_IMPLS = ("basic", "full_load_a", "full_load_b", "streamk")
 KERNEL_ENTRIES = {"basic": "ffn_fused_kernel (down: data-parallel tiles)",
-                  "streamk": "ffn_fused_kernel (down: data-parallel waves + Stream-K tail)"}
+                  "streamk": "ffn_fused_kernel (down: data-parallel waves + Stream-K tail)",
+                  "full_load_a": "ffn_rowblock_kernel (hidden row block resident on chip, N <= 256)"}
 
 
 class DependencyUnavailable(RuntimeError):
@@ -25,8 +26,10 @@ class NotApplicable(ValueError):
 class Selection:
     """Up/down implementation names (reference dispatch.py:42-66).
 
-    ``up_impl`` must be 'basic'; ``down_impl`` one of :data:`DOWN_IMPLS`.  The full-load
-    variants raise :class:`DependencyUnavailable` from :meth:`require_available`.
+    ``up_impl`` must be 'basic'; ``down_impl`` one of :data:`DOWN_IMPLS`.  'full_load_a'
+    (hidden row block resident on chip) applies when N <= 256 and otherwise raises
+    :class:`NotApplicable` at planning; 'full_load_b' raises :class:`DependencyUnavailable`
+    from :meth:`require_available`.
     """
 
     up_impl: str = "basic"
@@ -39,7 +42,7 @@ class Selection:
             raise ValueError(f"Unknown down_impl: {self.down_impl}")
 
     def require_available(self):
-        if self.down_impl in ("full_load_a", "full_load_b"):
+        if self.down_impl == "full_load_b":
             raise DependencyUnavailable(f"{self.down_impl}: not implemented in this build; no fallback")
         return self
 

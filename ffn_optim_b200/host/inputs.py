@@ -107,8 +107,9 @@ def prepare_storage(x, weight1, weight2, plan):
     of 8).  X is always copied into storage owned by the prepared FFN, as in the reference;
     weights that are already addressable are used in place.  Returns
     ``(x2d, w1, w2, hidden, out, workspace, counters, flags, status)``: x2d [M, ldx],
-    hidden [M, ldh] and out [M, ldy] with 16-byte pitches, fp32 workspace and u32/i32
-    synchronisation words (zeroed).
+    hidden [M, ldh] (for full_load_a only [M, 8]: the hidden tensor stays on chip) and
+    out [M, ldy] with 16-byte pitches, fp32 workspace and u32/i32 synchronisation words
+    (zeroed).
     """
     import torch
 
@@ -118,7 +119,10 @@ def prepare_storage(x, weight1, weight2, plan):
     x2d = _packed(xs, p.m, p.k)
     w1 = weight1 if _tma_ready(weight1, p.h, p.k) else _packed(weight1.contiguous(), p.h, p.k)
     w2 = weight2 if _tma_ready(weight2, p.n, p.h) else _packed(weight2.contiguous(), p.n, p.h)
-    hidden = torch.empty((p.m, pitch_of(p.h)), dtype=x.dtype, device=dev)
+    # full_load_a keeps the hidden row block on chip: an 8-column stand-in keeps the
+    # storage tuple's shape contract (row-indexable) without the M x H buffer.
+    on_chip = plan.selection.down_impl == "full_load_a"
+    hidden = torch.empty((p.m, 8 if on_chip else pitch_of(p.h)), dtype=x.dtype, device=dev)
     out = torch.empty((p.m, pitch_of(p.n)), dtype=x.dtype, device=dev)
     info = plan.kernel
     ws = torch.empty(max(int(info["workspace_floats"]), 4), dtype=torch.float32, device=dev)

@@ -138,6 +138,8 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
     info = _lib.PlanInfo()
     rc = lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info))
     if rc == _lib.ERR_NOT_APPLICABLE:
+        if selection.down_impl == "full_load_a":
+            raise NotApplicable("full_load_a keeps a 128 x N fp32 row block in TMEM: needs N <= 256")
         raise NotApplicable("Stream-K candidate has no remainder tiles for this block_num "
                             "or fewer than two K tiles")
     if rc == _lib.ERR_UNAVAILABLE:

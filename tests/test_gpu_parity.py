@@ -55,7 +55,7 @@ def run(x, w1, w2, **kw):
 
 
 @pytest.mark.parametrize("case_id", SMALL)
-@pytest.mark.parametrize("down_impl", ["basic", "streamk"])
+@pytest.mark.parametrize("down_impl", ["basic", "streamk", "full_load_a"])
 def test_small_cases_vs_reference_golden(case_id, down_impl):
     case = C.get_case(case_id)
     fx = np.load(GOLDEN / f"{case_id}.npz")
@@ -64,8 +64,8 @@ def test_small_cases_vs_reference_golden(case_id, down_impl):
     try:
         prepared, y = run(x, w1, w2, down_impl=down_impl)
     except NotApplicable:
-        assert down_impl == "streamk"
-        pytest.skip("Stream-K not applicable (no tail wave)")
+        assert down_impl == "streamk" or (down_impl == "full_load_a" and case["weight2_shape"][0] > 256)
+        pytest.skip(f"{down_impl} not applicable")
     assert tuple(y.shape) == C.case_problem(case).output_shape and y.dtype == x.dtype
     got = rows_of(y, fx["rows"])
     assert_close_bits(got, fx["staged_rational"], dt)
@@ -223,6 +223,56 @@ def test_ragged_shapes_vs_oracle(shape, down_impl, tile):
     f = lambda t: t.float().numpy()  # noqa: E731
     ref = O.ffn(f(x), f(w1), f(w2), dt, staged=True, rational=True)
     assert_close_bits(bits_of(y), ref, dt)
+
+
+RAGGED_N256 = [s for s in [
+    (1, 8, 8, 8, torch.bfloat16), (16, 64, 128, 128, torch.float16), (17, 72, 200, 136, torch.bfloat16),
+    (64, 4096, 384, 256, torch.bfloat16), (65, 96, 520, 72, torch.float16), (129, 136, 264, 264, torch.bfloat16),
+    (1000, 100, 1000, 250, torch.float16), (2048, 512, 1024, 200, torch.bfloat16), (300, 1000, 1500, 64, torch.bfloat16),
+    (4500, 40, 72, 129, torch.float16)]]
+
+
+@pytest.mark.parametrize("shape", RAGGED_N256, ids=lambda s: "x".join(map(str, s[:4])) + str(s[4])[-4:])
+@pytest.mark.parametrize("block_num", [None, 3])
+def test_full_load_a_vs_oracle(shape, block_num):
+    """Hidden-resident row blocks against the oracle (its H sum runs in 128-column chunks;
+    the oracle's in one pass: within the same two-ulp bound), ragged in every dimension,
+    one CTA per row block or several row blocks per CTA; N > 256 is not applicable."""
+    m, k, h, n, dtype = shape
+    g = torch.Generator().manual_seed(m * 13 + n)
+    x = torch.randn(m, k, generator=g).to(dtype)
+    w1 = (torch.randn(h, k, generator=g) * k ** -0.5).to(dtype)
+    w2 = (torch.randn(n, h, generator=g) * h ** -0.5).to(dtype)
+    if n > 256:
+        with pytest.raises(NotApplicable):
+            prepare_ffn(x.cuda(), w1.cuda(), w2.cuda(), down_impl="full_load_a")
+        return
+    prepared, y = run(x.cuda(), w1.cuda(), w2.cuda(), down_impl="full_load_a", block_num=block_num)
+    assert prepared.plan.kernel["variant"] in (7, 8, 9) and prepared.storage[3].shape[1] == 8
+    dt = str(dtype).removeprefix("torch.")
+    f = lambda t: t.float().numpy()  # noqa: E731
+    ref = O.ffn(f(x), f(w1), f(w2), dt, staged=True, rational=True)
+    assert_close_bits(bits_of(y), ref, dt)
+    first = bits_of(y)
+    prepared.run()
+    prepared.check()
+    assert np.array_equal(bits_of(y), first)
+
+
+@pytest.mark.parametrize("case_id", ["cfg2_fp16", "cfg2_bf16"])
+@pytest.mark.parametrize("gelu", ["rational", "erf"])
+def test_full_load_a_cfg2_vs_reference_golden(case_id, gelu):
+    case = C.get_case(case_id)
+    fx = np.load(GOLDEN / f"{case_id}.npz")
+    dt = str(fx["dtype"])
+    x, w1, w2 = C.make_inputs(case, device="cuda")
+    _, y = run(x, w1, w2, down_impl="full_load_a", gelu=gelu)
+    got = rows_of(y, fx["rows"])
+    assert_criterion(got, fx["golden"], dt)
+    if gelu == "rational":
+        assert_close_bits(got, fx["staged_rational"], dt)
+    else:
+        assert_close_bits(got, fx["golden"], dt, floor=4e-3)
 
 
 @pytest.mark.parametrize("block_num", [1, 3, 37, 148])

@@ -92,9 +92,22 @@ def test_max_abs_bound_is_strict_only():
 
 # ---------------------------------------------------------------- selection and planning
 def test_selection():
-    for kind in ("full_load_a", "full_load_b"):
-        with pytest.raises(DependencyUnavailable):
-            Selection(down_impl=kind).require_available()
+    with pytest.raises(DependencyUnavailable):
+        Selection(down_impl="full_load_b").require_available()
+    Selection(down_impl="full_load_a").require_available()
+    # full_load_a: hidden row block on chip, Y row block in TMEM -> N <= 256 (BASELINE cfg2 yes, cfg1 no)
+    cfg2 = problem_from_shapes([6993, 100], [1000, 100], [250, 1000])
+    plan = make_plan(cfg2, Selection(down_impl="full_load_a"), sm_count=148)
+    assert plan.kernel["variant"] == 9 and plan.block_num == 55 and plan.kernel["tile_n"] == 256
+    assert plan.kernel["up"]["tiles_q"] == 8 and plan.kernel["up"]["k_blocks"] == 2
+    assert make_plan(cfg2, Selection(down_impl="full_load_a"), 16, sm_count=148).block_num == 16
+    with pytest.raises(NotApplicable):
+        make_plan(problem_from_shapes([512, 512], [2048, 512], [512, 2048]), Selection(down_impl="full_load_a"),
+                  sm_count=148)
+    with pytest.raises(ValueError):  # a two-phase tile cannot run full_load_a, nor the reverse
+        make_plan(cfg2, Selection(down_impl="full_load_a"), sm_count=148, tile="cta128x256")
+    with pytest.raises(ValueError):
+        make_plan(cfg2, Selection(down_impl="basic"), sm_count=148, tile="rowblock256")
     with pytest.raises(ValueError):
         Selection(up_impl="streamk")
     with pytest.raises(ValueError):
@@ -254,8 +267,10 @@ def test_c_planner_rejects_bad_problems(lib):
     for m, k, h, n, dt, down in [(0, 8, 8, 8, 1, 0), (8, 70000, 8, 8, 1, 0), (8, 8, 8, 8, 5, 0), (8, 8, 8, 8, 1, 9)]:
         prob = _lib.Problem(m, k, h, n, dt, down, 0, 0, 148)
         assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_INVALID
-    prob = _lib.Problem(64, 64, 64, 64, 1, 1, 0, 0, 148)
+    prob = _lib.Problem(64, 64, 64, 64, 1, 2, 0, 0, 148)  # full_load_b
     assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_UNAVAILABLE
+    prob = _lib.Problem(64, 64, 64, 300, 1, 1, 0, 0, 148)  # full_load_a with N > 256
+    assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_NOT_APPLICABLE
     # prepare without a usable device fails cleanly (no GPU in the CPU suite, or bad pointers)
     bufs = _lib.Buffers()
     h = ctypes.c_void_p()

@@ -28,6 +28,9 @@ SHAPES = [
     (16, 4096, 16384, 4096, torch.bfloat16, "streamk"),   # decode-sized (BASELINE cfg3)
     (256, 192, 520, 136, torch.bfloat16, "streamk"),
     (512, 512, 2048, 512, torch.float16, "basic"),        # BASELINE cfg1 shape
+    (6993, 104, 1000, 250, torch.float16, "full_load_a"),  # BASELINE cfg2 shape (K padded to a
+                                                            # 16-byte pitch), hidden on chip
+    (4096, 64, 8192, 64, torch.bfloat16, "full_load_a"),   # hidden would be 64 MiB: none needed
 ]
 
 
