@@ -443,6 +443,68 @@ __device__ __forceinline__ float gelu(float z) {
   if constexpr (GELU == 0) return gelu_rational(z);
   else return gelu_erf(z);
 }
+// Packed fp32 pairs (sm_100 fma/mul/add .f32x2): each lane is one IEEE fp32 operation
+// rounded to nearest, so a pair evaluates exactly what two scalar operations would.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_splat(float c) { return f2_pack(c, c); }
+// gelu_rational on two values at once: the same operations in the same order (the clip
+// and the division per lane), with the Horner steps and products packed.
+__device__ __forceinline__ void gelu_rational2(float& z0, float& z1) {
+  const uint64_t z = f2_pack(z0, z1);
+  float t0, t1;
+  f2_unpack(f2_mul(z, f2_splat(0.70710678118654752f)), t0, t1);
+  t0 = fminf(fmaxf(t0, -3.92f), 3.92f);
+  t1 = fminf(fmaxf(t1, -3.92f), 3.92f);
+  const uint64_t t = f2_pack(t0, t1);
+  const uint64_t t2 = f2_mul(t, t);
+  uint64_t p = f2_fma(t2, f2_splat(0.053443748819f), f2_splat(7.5517016694f));
+  p = f2_fma(p, t2, f2_splat(101.62808918f));
+  p = f2_fma(p, t2, f2_splat(1393.8061484f));
+  p = f2_fma(p, t2, f2_splat(5063.7915060f));
+  p = f2_fma(p, t2, f2_splat(29639.384698f));
+  p = f2_mul(p, t);
+  uint64_t q = f2_add(t2, f2_splat(31.212858877f));
+  q = f2_fma(q, t2, f2_splat(398.56963806f));
+  q = f2_fma(q, t2, f2_splat(3023.1248150f));
+  q = f2_fma(q, t2, f2_splat(13243.365831f));
+  q = f2_fma(q, t2, f2_splat(26267.224157f));
+  float p0, p1, q0, q1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(q, q0, q1);
+  const uint64_t r = f2_pack(1.0f + __fdividef(p0, q0), 1.0f + __fdividef(p1, q1));
+  f2_unpack(f2_mul(f2_mul(f2_splat(0.5f), z), r), z0, z1);
+}
+template <int GELU>
+__device__ __forceinline__ void gelu2(float& a, float& b) {
+  if constexpr (GELU == 0) {
+    gelu_rational2(a, b);
+  } else {
+    a = gelu_erf(a);
+    b = gelu_erf(b);
+  }
+}
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   if constexpr (BF16) {
@@ -1110,7 +1172,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
           }
           if (u.phase == 0) {
 #pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] = gelu<GELU>(v[j]);
+            for (int j = 0; j < 64; j += 2) gelu2<GELU>(v[j], v[j + 1]);
           }
           if (rs_reduce) {
             // Ascending rank order: sum = p_0 + p_1 + ... (this rank's fp32 partial in place),

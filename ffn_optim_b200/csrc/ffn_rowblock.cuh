@@ -279,7 +279,10 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 8, 1) ffn_rowblock_kernel(
         ++ucnt;
         uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = pack2<BF16>(gelu<GELU>(v[2 * i]), gelu<GELU>(v[2 * i + 1]));
+        for (int i = 0; i < 32; ++i) {
+          gelu2<GELU>(v[2 * i], v[2 * i + 1]);
+          pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
+        }
         const int b = hcnt & 1;
         ok = warp_wait(hempty(b), ((hcnt >> 1) & 1) ^ 1u, 420 + b);
         if (!ok) break;
