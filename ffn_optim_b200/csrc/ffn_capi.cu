@@ -45,8 +45,8 @@ struct Variant {
 constexpr Variant kVariants[] = {{256, 4, false, false, 1, 4, false}, {128, 4, false, false, 1, 8, false},
                                  {16, 8, true, false, 1, 8, false},   {64, 8, true, false, 1, 8, false},
                                  {256, 6, false, true, 1, 4, false},  {16, 3, true, false, 4, 8, false},
-                                 {64, 4, true, false, 2, 8, false},   {64, 4, false, false, 1, 8, true},
-                                 {128, 4, false, false, 1, 8, true},  {256, 4, false, false, 1, 8, true}};
+                                 {64, 4, true, false, 2, 8, false},   {64, 4, false, false, 1, 16, true},
+                                 {128, 4, false, false, 1, 16, true}, {256, 4, false, false, 1, 16, true}};
 constexpr int kNumVariants = 10;
 constexpr int kFirstRowblock = 7;
 

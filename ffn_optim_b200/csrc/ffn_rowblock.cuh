@@ -29,7 +29,7 @@ namespace ffnb200 {
 
 template <int NY, int STAGES>
 struct RowLayout {
-  static constexpr int kEpiWarps = 8;                   // two per TMEM sub-partition
+  static constexpr int kEpiWarps = 16;                  // four per TMEM sub-partition
   static constexpr int kThreads = kCtrlThreads + 32 * kEpiWarps;
   static constexpr int kChunk = 128;                    // H columns per up chunk
   static constexpr int kStage = 32768;                  // X + W1 k-block, or one W2 k-block
@@ -39,12 +39,12 @@ struct RowLayout {
   static constexpr int kTmemCols = 512;                 // up accumulators 0..255, Y 256..256+NY
   static_assert(NY == 64 || NY == 128 || NY == 256, "Y accumulator width");
   static_assert(NY * kBK * 2 <= kStage, "W2 k-block fits a stage");
-  static_assert((2 * STAGES + 11) * 8 + 8 <= kBarBytes, "barrier area");
+  static_assert((2 * STAGES + 12) * 8 + 8 <= kBarBytes, "barrier area");
   static_assert(kSmem <= 232448, "dynamic shared memory per CTA");
 };
 
 template <int NY, int STAGES, bool BF16, int GELU>
-__global__ void __launch_bounds__(kCtrlThreads + 32 * 8, 1) ffn_rowblock_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel(const __grid_constant__ Params p) {
   using LY = RowLayout<NY, STAGES>;
   constexpr uint32_t kIdescUp = make_idesc<BF16, LY::kChunk, kBM>();
   constexpr uint32_t kIdescDn = make_idesc<BF16, NY, kBM>();
@@ -67,7 +67,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 8, 1) ffn_rowblock_kernel(
   const uint32_t yfull = sBar + 8u * (2 * STAGES + 8);
   const uint32_t yempty = sBar + 8u * (2 * STAGES + 9);
   const uint32_t drain_bar = sBar + 8u * (2 * STAGES + 10);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (sBar - base) + 8 * (2 * STAGES + 11));
+  const uint32_t ystage_free = sBar + 8u * (2 * STAGES + 11);  // Y staging read by its TMA stores
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (sBar - base) + 8 * (2 * STAGES + 12));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -91,6 +92,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 8, 1) ffn_rowblock_kernel(
     mbar_init(yfull, 1);
     mbar_init(yempty, LY::kEpiWarps);
     mbar_init(drain_bar, 1);
+    mbar_init(ystage_free, LY::kEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
     fence_async_shared();
@@ -237,25 +239,34 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 8, 1) ffn_rowblock_kernel(
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..9)
-    const int ew = warp - kCtrlThreads / 32;  // 0..7
-    const int sub = warp & 3;           // TMEM lane sub-partition this warp may access
-    const int part = ew >> 2;           // which 64-column half of a chunk
+    // ---------------------------------------------------------------- epilogue (warps 2..17)
+    // Four warps per TMEM sub-partition; warp `part` of a sub-partition converts columns
+    // part*32 .. part*32+31 of each 128-column chunk for its 32 rows.
+    const int ew = warp - kCtrlThreads / 32;  // 0..15
+    const int sub = warp & 3;                 // TMEM lane sub-partition this warp may access
+    const int part = ew >> 2;                 // 32-column quarter of a chunk
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
-    // This warp's 4 KB region in hidden buffer b: k-block `part`, rows sub*32.. (32 x 128 B).
-    auto region = [&](int b) { return sH + static_cast<uint32_t>(b * LY::kHidBuf + part * kABytes + sub * 32 * 128); };
+    const int row = sub * 32 + lane;          // row of the block
+    // This warp's 64-byte half rows of hidden buffer b: k-block part/2, 16-byte chunks
+    // (part&1)*4 .. +3 of row `row` (128B-swizzled, the MMA's K-major A layout).
+    auto hid_row = [&](int b) {
+      return sH + static_cast<uint32_t>(b * LY::kHidBuf + (part >> 1) * kABytes + row * 128);
+    };
+    // Y staging: 4 KB per warp (32 rows x 128 B) over the idle hidden buffers.
+    const uint32_t ystage = sH + static_cast<uint32_t>(ew * 4096);
     int ucnt = 0, hcnt = 0, rcnt = 0;
-    bool stores_pending = false;
+    bool y_staged = false;  // this CTA's last Y staging may still be read by TMA stores
     int ok = 1;
     auto warp_wait = [&](uint32_t bar, uint32_t par, int aux) {
       int r = 1;
       if (lane == 0) r = wait_bar(bar, par, abort_flag, p, aux) ? 1 : 0;
       return __shfl_sync(0xffffffffu, r, 0);
     };
-    auto store_swizzled = [&](uint32_t reg, const uint32_t* pk) {
+    // 16 packed words = 32 columns as four swizzled 16-byte chunks c0..c0+3 of a 128-byte row.
+    auto store_quarter = [&](uint32_t row_addr, int swz_row, int c0, const uint32_t* pk) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t addr = reg + lane * 128 + ((c ^ (lane & 7)) << 4);
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t addr = row_addr + (((c0 + c) ^ (swz_row & 7)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
                      "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
                      : "memory");
@@ -269,64 +280,66 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 8, 1) ffn_rowblock_kernel(
         ok = warp_wait(ufull(a), (ucnt >> 1) & 1, 400 + a);
         if (!ok) break;
         tc_fence_after();
-        float v[64];
-        const uint32_t t = tmem_base + lane_off + static_cast<uint32_t>(a * LY::kChunk + part * 64);
-        tmem_ld32(t, v);
-        tmem_ld32(t + 32, v + 32);
+        float v[32];
+        tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(a * LY::kChunk + part * 32), v);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(uempty(a));
         ++ucnt;
-        uint32_t pk[32];
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 16; ++i) {
           gelu2<GELU>(v[2 * i], v[2 * i + 1]);
           pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
         }
         const int b = hcnt & 1;
         ok = warp_wait(hempty(b), ((hcnt >> 1) & 1) ^ 1u, 420 + b);
-        if (!ok) break;
-        if (stores_pending) {  // Y stores of the previous row block read this region
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          stores_pending = false;
+        if (ok && y_staged) {  // every warp's Y stores have read the staging this write overlaps
+          ok = warp_wait(ystage_free, (rcnt - 1) & 1, 460);
+          y_staged = false;
         }
-        store_swizzled(region(b), pk);
+        if (!ok) break;
+        store_quarter(hid_row(b), row, (part & 1) * 4, pk);
         fence_async_shared();
         __syncwarp();
         if (lane == 0) mbar_arrive(hfull(b));
         ++hcnt;
       }
       if (!ok) break;
-      // Y of the row block: 64-column chunks split over the two warps of a sub-partition,
-      // staged in this warp's own regions of the (now idle) hidden buffers.
+      // Y of the row block: 64-column chunks, one per warp of a sub-partition (NY <= 256).
       ok = warp_wait(yfull, rcnt & 1, 440);
       if (!ok) break;
       tc_fence_after();
-      int used = 0;
-#pragma unroll 1
-      for (int yc = part; yc < NY / 64 && yc * 64 < p.N; yc += 2) {
-        float v[64];
-        const uint32_t t = tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64);
-        tmem_ld32(t, v);
-        tmem_ld32(t + 32, v + 32);
-        uint32_t pk[32];
+      const int yc = part;
+      const bool mine = yc < NY / 64 && yc * 64 < p.N;
+      if (mine) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
-        const uint32_t reg = region(used);
-        store_swizzled(reg, pk);
-        fence_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&p.tm_st_y, reg, yc * 64, rb * kBM + sub * 32);
-          bulk_commit();
+        for (int h = 0; h < 2; ++h) {
+          float v[32];
+          tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), v);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
+          store_quarter(ystage + lane * 128, lane, h * 4, pk);
         }
-        ++used;
       }
-      stores_pending = used > 0;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(yempty);
+      if (mine) {
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&p.tm_st_y, ystage, yc * 64, rb * kBM + sub * 32);
+          bulk_commit();
+        }
+      }
+      if (lane == 0) {
+        bulk_wait_read0();
+        mbar_arrive(ystage_free);
+      }
+      __syncwarp();
+      y_staged = true;
       ++rcnt;
     }
     if (lane == 0) bulk_wait_all();
