@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--tile", default=None, help="force a kernel variant (see ffn_optim_b200._lib.TILE_VARIANTS)")
     ap.add_argument("--down-impl", choices=("basic", "streamk", "full_load_a"), default=None,
                     help="override the workload's down_impl")
+    ap.add_argument("--weights", choices=("native", "fp8"), default="native",
+                    help="fp8: e4m3 weights with per-row scales, widened on chip (decode tiles, M <= 64)")
     ap.add_argument("--schedule", choices=("static", "dynamic"), default=None,
                     help="data-parallel tile order (default: dynamic for CTA-pair tiles, static otherwise)")
     ap.add_argument("--cpu-rows", type=int, default=1024)
@@ -277,7 +279,8 @@ def main():
     down = args.down_impl or case.get("down_impl", "basic")
 
     if world == 1:
-        runner = prepare_ffn(x, w1, w2, down_impl=down, tile=args.tile, schedule=args.schedule)
+        runner = prepare_ffn(x, w1, w2, down_impl=down, tile=args.tile, schedule=args.schedule,
+                             weight_format=None if args.weights == "native" else args.weights)
         launches = 1
         kernel_runs = lambda: runner.run()  # noqa: E731
         check = runner.check
@@ -381,7 +384,7 @@ def main():
                "api": f"PreparedFFN.run_host(pinned X, pinned Y, chunks={chunks})", "gpu_launches": chunks * args.steps}
 
     cpu = None
-    if world == 1 and rank == 0 and not args.no_cpu:
+    if world == 1 and rank == 0 and not args.no_cpu and args.weights == "native":
         rows = min(args.cpu_rows, p.m)
         xb = to_bits(x.reshape(p.m, p.k)[:rows])
         w1b = to_bits(runner.storage[1][:, :p.k])
@@ -410,6 +413,7 @@ def main():
                            "down_impl": down, "parallelism": parallelism,
                            "block_num": block_num, "kernel_variant": variant,
                            "schedule": {1: "static", 2: "dynamic"}.get(first.plan.kernel.get("schedule")),
+                           "weights": args.weights,
                            "l2": "L2 flushed between steps (512 MB write)" if flush else "inputs larger than L2, no flush"},
                 "gpu_launches": launches * args.steps, "clocks": clocks, "roofline": roofline,
                 "e2e": e2e, "cpu_baseline": cpu}

@@ -30,18 +30,21 @@ DOWN_IMPL_CODES = {"basic": 0, "full_load_a": 1, "full_load_b": 2, "streamk": 3}
 GELU_CODES = {"rational": 0, "erf": 1}
 # Kernel variants selectable through prepare_ffn(..., tile=...) (None = automatic).
 TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5,
-                 "swap16k4": 6, "swap64k2": 7, "rowblock64": 8, "rowblock128": 9, "rowblock256": 10}
+                 "swap16k4": 6, "swap64k2": 7, "rowblock64": 8, "rowblock128": 9, "rowblock256": 10,
+                 "swap16fp8": 11, "swap64fp8": 12}
+WEIGHT_FORMATS = {"native": 0, "fp8": 1}
 L2_POLICIES = {"none": 1, "stream_b": 2, "normal": 3, "keep_a": 4}
 SCHEDULES = {"static": 1, "dynamic": 2}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",
                  3: "Stream-K partial wait timed out", 4: "peer GPU partial wait timed out (fused reduce-scatter)",
-                 5: "tile claim out of range (counters not reset after an earlier error)"}
+                 5: "tile claim out of range (counters not reset after an earlier error)",
+                 6: "activation beyond the fp16 range of the fp8-weight path (|x| > 65504)"}
 
 # Every symbol the header declares; the CPU tests check the library exports all of them.
 EXPORTED = ("ffn_b200_abi_version", "ffn_b200_strerror", "ffn_b200_device_info", "ffn_b200_make_plan",
             "ffn_b200_prepare", "ffn_b200_run", "ffn_b200_rebind_io", "ffn_b200_reset",
             "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_set_trace",
-            "ffn_b200_set_owner_map", "ffn_b200_get_owner_map", "ffn_b200_get_plan",
+            "ffn_b200_set_owner_map", "ffn_b200_get_owner_map", "ffn_b200_quantize_fp8_rows", "ffn_b200_get_plan",
             "ffn_b200_destroy", "ffn_b200_launch", "ffn_b200_run_noalloc", "ffn_b200_peer_alloc",
             "ffn_b200_peer_open", "ffn_b200_peer_close", "ffn_b200_peer_free", "ffn_b200_reduce_scatter_bytes",
             "ffn_b200_set_reduce_scatter")
@@ -51,7 +54,8 @@ class Problem(ctypes.Structure):
     _fields_ = [("m", ctypes.c_int64), ("k", ctypes.c_int64), ("h", ctypes.c_int64), ("n", ctypes.c_int64),
                 ("dtype", ctypes.c_int32), ("down_impl", ctypes.c_int32), ("gelu", ctypes.c_int32),
                 ("block_num", ctypes.c_int32), ("sm_count", ctypes.c_int32), ("tile_variant", ctypes.c_int32),
-                ("raster_group", ctypes.c_int32), ("l2_policy", ctypes.c_int32), ("schedule", ctypes.c_int32)]
+                ("raster_group", ctypes.c_int32), ("l2_policy", ctypes.c_int32), ("schedule", ctypes.c_int32),
+                ("weight_format", ctypes.c_int32)]
 
 
 class PhasePlan(ctypes.Structure):
@@ -85,7 +89,8 @@ class Buffers(ctypes.Structure):
                 ("w2", ctypes.c_void_p), ("ldw2", ctypes.c_int64), ("hidden", ctypes.c_void_p),
                 ("ldh", ctypes.c_int64), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
                 ("workspace", ctypes.c_void_p), ("counters", ctypes.c_void_p), ("flags", ctypes.c_void_p),
-                ("status", ctypes.c_void_p)]
+                ("status", ctypes.c_void_p),
+                ("w1_scale", ctypes.c_void_p), ("w2_scale", ctypes.c_void_p)]
 
 
 _lock = threading.Lock()
@@ -127,6 +132,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             "ffn_b200_set_trace": ([vp, vp], i32),
             "ffn_b200_set_owner_map": ([vp, vp], i32),
             "ffn_b200_get_owner_map": ([vp, vp, i32, vp], i32),
+            "ffn_b200_quantize_fp8_rows": ([vp, i64, i32, i64, i64, vp, i64, vp, vp], i32),
             "ffn_b200_get_plan": ([vp, ctypes.POINTER(PlanInfo)], i32),
             "ffn_b200_destroy": ([vp], i32),
             "ffn_b200_launch": ([ctypes.POINTER(Problem), ctypes.POINTER(Buffers), vp], i32),

@@ -13,7 +13,7 @@ from time import perf_counter
 
 from . import _lib
 from .host.dispatch import Selection, kernel_provenance
-from .host.inputs import prepare_storage, validate_tensors
+from .host.inputs import prepare_storage, quantize_weights_fp8, validate_tensors
 from .host.tiling import make_plan, problem_struct
 
 
@@ -43,6 +43,7 @@ class PreparedFFN:
     provenance: dict
     preparation: dict
     stream: object
+    weight_scales: tuple = None  # fp8 weights: (W1 row scales [H], W2 row scales [N]); storage[1:3] hold the codes
 
     def _output_view(self):
         p = self.plan.problem
@@ -98,17 +99,20 @@ class PreparedFFN:
             sms = torch.cuda.get_device_properties(dev).multi_processor_count
             plan = make_plan(sub, self.plan.selection, self.plan.block_num, gelu=self.plan.gelu, sm_count=sms,
                              tile=o.get("tile"), raster_group=o.get("raster_group"), l2_policy=o.get("l2_policy"),
-                             schedule=o.get("schedule"))
+                             schedule=o.get("schedule"), weight_format=o.get("weight_format"))
             k = plan.kernel
             if k["workspace_floats"] > ws.numel():
                 ws = torch.empty(int(k["workspace_floats"]), dtype=torch.float32, device=dev)
             sync = torch.zeros(int(k["counter_words"]) + int(k["flag_words"]) + 4, dtype=torch.int32, device=dev)
             cnt, flg, st = sync[:k["counter_words"]], sync[k["counter_words"]:-4], sync[-4:]
+            sc = self.weight_scales
             bufs = _lib.Buffers(x2d[lo].data_ptr(), x2d.stride(0), w1.data_ptr(), w1.stride(0), w2.data_ptr(),
                                 w2.stride(0), hidden[lo].data_ptr(), hidden.stride(0), out[lo].data_ptr(),
-                                out.stride(0), ws.data_ptr(), cnt.data_ptr(), flg.data_ptr(), st.data_ptr())
+                                out.stride(0), ws.data_ptr(), cnt.data_ptr(), flg.data_ptr(), st.data_ptr(),
+                                sc[0].data_ptr() if sc else None, sc[1].data_ptr() if sc else None)
             prob = problem_struct(sub, self.plan.selection.down_impl, self.plan.gelu, plan.block_num, sms,
-                                  o.get("tile"), o.get("raster_group"), o.get("l2_policy"), o.get("schedule"))
+                                  o.get("tile"), o.get("raster_group"), o.get("l2_policy"), o.get("schedule"),
+                                  o.get("weight_format"))
             h = ctypes.c_void_p()
             rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), dev.index or 0, ctypes.byref(h))
             if rc != _lib.OK:
@@ -296,7 +300,8 @@ def _map_prepare_error(rc):
 
 
 def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", block_num=None,
-                layout="linear", gelu="rational", tile=None, raster_group=None, l2_policy=None, schedule=None):
+                layout="linear", gelu="rational", tile=None, raster_group=None, l2_policy=None, schedule=None,
+                weight_format=None):
     """Validates, plans and prepares storage and the launch handle without launching the FFN
     (reference ops/api.py:48-89).
 
@@ -304,8 +309,11 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
     SMs).  ``gelu`` selects the epilogue GELU: 'rational' (the reference kernel's clipped
     rational erf) or 'erf' (CUDA ``erff``).  ``tile`` forces a kernel variant (see
     ``make_plan``); None chooses automatically; ``raster_group``, ``l2_policy`` and
-    ``schedule`` are tuning overrides passed to ``make_plan``.  Storage copies are device
-    work timed separately as ``preparation['auxiliary_device_interval_ms']``.
+    ``schedule`` are tuning overrides passed to ``make_plan``.  ``weight_format='fp8'``
+    (decode, M <= 64) quantizes W1 and W2 once to e4m3 codes with per-row fp32 scales
+    (``quantize_weights_fp8``) and runs the tiles that widen them on chip: half the weight
+    bytes, a weight-quantization error on top of the reference arithmetic.  Storage copies
+    are device work timed separately as ``preparation['auxiliary_device_interval_ms']``.
     """
     import torch
 
@@ -317,7 +325,7 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
         raise KernelCompilationError(f"{type(exc).__name__}: {exc}") from exc
     props = torch.cuda.get_device_properties(x.device)
     plan = make_plan(p, selection, block_num, gelu=gelu, sm_count=props.multi_processor_count, tile=tile,
-                     raster_group=raster_group, l2_policy=l2_policy, schedule=schedule)
+                     raster_group=raster_group, l2_policy=l2_policy, schedule=schedule, weight_format=weight_format)
     if (props.major, props.minor) != (10, 0):
         raise RuntimeError("This implementation targets B200 (sm_100) only")
     if plan.block_num > props.multi_processor_count:
@@ -326,6 +334,11 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
         stream = torch.cuda.current_stream()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
+        scales = None
+        if weight_format == "fp8":
+            q1, s1 = quantize_weights_fp8(weight1)
+            q2, s2 = quantize_weights_fp8(weight2)
+            weight1, weight2, scales = q1[:, :p.k], q2[:, :p.h], (s1, s2)
         storage = prepare_storage(x, weight1, weight2, plan)
         end.record()
         end.synchronize()
@@ -333,9 +346,10 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
         x2d, w1, w2, hidden, out, ws, counters, flags, status = storage
         bufs = _lib.Buffers(x2d.data_ptr(), x2d.stride(0), w1.data_ptr(), w1.stride(0), w2.data_ptr(), w2.stride(0),
                             hidden.data_ptr(), hidden.stride(0), out.data_ptr(), out.stride(0), ws.data_ptr(),
-                            counters.data_ptr(), flags.data_ptr(), status.data_ptr())
+                            counters.data_ptr(), flags.data_ptr(), status.data_ptr(),
+                            scales[0].data_ptr() if scales else None, scales[1].data_ptr() if scales else None)
         prob = problem_struct(p, down_impl, gelu, plan.block_num, props.multi_processor_count, tile, raster_group,
-                              l2_policy, schedule)
+                              l2_policy, schedule, weight_format)
         handle = ctypes.c_void_p()
         before = perf_counter()
         rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), x.device.index or 0, ctypes.byref(handle))
@@ -345,7 +359,7 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
                        "compile_wall_ms": (perf_counter() - before) * 1000}
     provenance = kernel_provenance(down_impl)
     provenance["plan"] = plan.kernel
-    return PreparedFFN(plan, storage, handle, provenance, preparation, stream)
+    return PreparedFFN(plan, storage, handle, provenance, preparation, stream, scales)
 
 
 def ffn(x, weight1, weight2, **configuration):

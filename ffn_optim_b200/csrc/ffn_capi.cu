@@ -37,34 +37,40 @@ struct Variant {
   int ksub;       // 64-wide K sub-blocks per pipeline stage
   int epi;        // epilogue warps (4, or 8 = two per TMEM sub-partition for short tiles)
   bool rowblock;  // hidden-resident row-block kernel (down_impl full_load_a); bn = Y width
+  bool w8;        // fp8 weights widened on chip by 4 converter warps (decode tiles)
 };
 // 0: prefill tiles 128x256 (one CTA), 1: 128x128 for small grids, 2/3: swap-AB decode
 // tiles (16 / 64 tokens), 4: prefill tiles 256x256 computed by a CTA pair (cta_group::2),
 // 5/6: swap-AB decode tiles with 256/128-wide K stages (longer contiguous weight reads),
-// 7/8/9: hidden-resident row blocks with a 64/128/256-column Y accumulator.
-constexpr Variant kVariants[] = {{256, 4, false, false, 1, 4, false}, {128, 4, false, false, 1, 8, false},
-                                 {16, 8, true, false, 1, 8, false},   {64, 8, true, false, 1, 8, false},
-                                 {256, 6, false, true, 1, 4, false},  {16, 3, true, false, 4, 8, false},
-                                 {64, 4, true, false, 2, 8, false},   {64, 4, false, false, 1, 16, true},
-                                 {128, 4, false, false, 1, 16, true}, {256, 4, false, false, 1, 16, true}};
-constexpr int kNumVariants = 10;
+// 7/8/9: hidden-resident row blocks with a 64/128/256-column Y accumulator,
+// 10/11: swap-AB decode tiles (16 / 64 tokens) with fp8 weights.
+constexpr Variant kVariants[] = {
+    {256, 4, false, false, 1, 4, false, false}, {128, 4, false, false, 1, 8, false, false},
+    {16, 8, true, false, 1, 8, false, false},   {64, 8, true, false, 1, 8, false, false},
+    {256, 6, false, true, 1, 4, false, false},  {16, 3, true, false, 4, 8, false, false},
+    {64, 4, true, false, 2, 8, false, false},   {64, 4, false, false, 1, 16, true, false},
+    {128, 4, false, false, 1, 16, true, false}, {256, 4, false, false, 1, 16, true, false},
+    {16, 6, true, false, 2, 8, false, true},    {64, 4, true, false, 2, 8, false, true}};
+constexpr int kNumVariants = 12;
 constexpr int kFirstRowblock = 7;
 
-template <int BN, int ST, bool SW, bool PR, int KS, int EP>
+template <int BN, int ST, bool SW, bool PR, int KS, int EP, bool W8>
 KernelFn pick_kernel(int bf16, int gelu) {
   using namespace ffnb200;
   if (bf16)
-    return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, EP, true, 1> : ffn_fused_kernel<BN, ST, SW, PR, KS, EP, true, 0>;
-  return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, EP, false, 1> : ffn_fused_kernel<BN, ST, SW, PR, KS, EP, false, 0>;
+    return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, EP, true, 1, W8> : ffn_fused_kernel<BN, ST, SW, PR, KS, EP, true, 0, W8>;
+  return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, EP, false, 1, W8> : ffn_fused_kernel<BN, ST, SW, PR, KS, EP, false, 0, W8>;
 }
 #define FFN_B200_VARIANTS(X)                  \
-  X(0, 256, 4, false, false, 1, 4)            \
-  X(1, 128, 4, false, false, 1, 8)            \
-  X(2, 16, 8, true, false, 1, 8)              \
-  X(3, 64, 8, true, false, 1, 8)              \
-  X(4, 256, 6, false, true, 1, 4)             \
-  X(5, 16, 3, true, false, 4, 8)              \
-  X(6, 64, 4, true, false, 2, 8)
+  X(0, 256, 4, false, false, 1, 4, false)     \
+  X(1, 128, 4, false, false, 1, 8, false)     \
+  X(2, 16, 8, true, false, 1, 8, false)       \
+  X(3, 64, 8, true, false, 1, 8, false)       \
+  X(4, 256, 6, false, true, 1, 4, false)      \
+  X(5, 16, 3, true, false, 4, 8, false)       \
+  X(6, 64, 4, true, false, 2, 8, false)       \
+  X(10, 16, 6, true, false, 2, 8, true)       \
+  X(11, 64, 4, true, false, 2, 8, true)
 template <int NY>
 KernelFn pick_rowblock(int bf16, int gelu) {
   using namespace ffnb200;
@@ -73,8 +79,8 @@ KernelFn pick_rowblock(int bf16, int gelu) {
 }
 KernelFn kernel_for(int variant, int bf16, int gelu) {
   switch (variant) {
-#define X(id, bn, st, sw, pr, ks, ep) \
-  case id: return pick_kernel<bn, st, sw, pr, ks, ep>(bf16, gelu);
+#define X(id, bn, st, sw, pr, ks, ep, w8) \
+  case id: return pick_kernel<bn, st, sw, pr, ks, ep, w8>(bf16, gelu);
     FFN_B200_VARIANTS(X)
 #undef X
     case 7: return pick_rowblock<64>(bf16, gelu);
@@ -85,8 +91,8 @@ KernelFn kernel_for(int variant, int bf16, int gelu) {
 }
 int smem_for(int variant) {
   switch (variant) {
-#define X(id, bn, st, sw, pr, ks, ep) \
-  case id: return ffnb200::Layout<bn, st, sw, pr, ks, ep>::kSmem;
+#define X(id, bn, st, sw, pr, ks, ep, w8) \
+  case id: return ffnb200::Layout<bn, st, sw, pr, ks, ep, w8>::kSmem;
     FFN_B200_VARIANTS(X)
 #undef X
     case 7: return ffnb200::RowLayout<64, 4>::kSmem;
@@ -95,11 +101,17 @@ int smem_for(int variant) {
   }
   return 0;
 }
-int threads_for(int variant) { return ffnb200::kCtrlThreads + 32 * kVariants[variant].epi; }
+int threads_for(int variant) {
+  return ffnb200::kCtrlThreads + 32 * (kVariants[variant].epi + (kVariants[variant].w8 ? 12 : 0));
+}
 int tmem_cols_for(int variant) {
-  if (kVariants[variant].rowblock) return 512;
-  const int c = 2 * kVariants[variant].bn;
-  return c < 32 ? 32 : c;
+  switch (variant) {
+#define X(id, bn, st, sw, pr, ks, ep, w8) \
+  case id: return ffnb200::Layout<bn, st, sw, pr, ks, ep, w8>::kTmemCols;
+    FFN_B200_VARIANTS(X)
+#undef X
+  }
+  return 512;  // row-block variants
 }
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -229,6 +241,24 @@ int encode_2d(CUtensorMap* tm, const void* base, int dtype, int64_t inner, int64
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 2-D row-major tensor of fp8 codes [outer, inner] (inner even), pitch in bytes, described to
+// the TMA as pairs of codes (16-bit elements: the copy engine's work follows the element
+// count, and the bytes and their swizzled placement are the same); box_inner in bytes; the
+// swizzle spans the box row (64- or 128-byte rows).
+int encode_2d_u8(CUtensorMap* tm, const void* base, int64_t inner, int64_t outer, int64_t pitch, uint32_t box_inner,
+                 uint32_t box_outer) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner / 2), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+  cuuint32_t box[2] = {box_inner / 2, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        box_inner >= 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FFN_B200_OK : FFN_B200_ERR_CUDA;
+}
+
 }  // namespace
 
 struct ffn_b200_handle {
@@ -294,15 +324,28 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   if (pr->tile_variant < 0 || pr->tile_variant > kNumVariants) return FFN_B200_ERR_INVALID;
   if (pr->raster_group < 0 || pr->l2_policy < 0 || pr->l2_policy > 4) return FFN_B200_ERR_INVALID;
   if (pr->schedule < 0 || pr->schedule > 2) return FFN_B200_ERR_INVALID;
+  if (pr->weight_format != FFN_B200_WEIGHTS_NATIVE && pr->weight_format != FFN_B200_WEIGHTS_FP8_ROWS)
+    return FFN_B200_ERR_INVALID;
+  const bool fp8w = pr->weight_format == FFN_B200_WEIGHTS_FP8_ROWS;
 
   std::memset(out, 0, sizeof(*out));
-  if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_A) return plan_rowblock(*pr, grid, out);
+  if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_A) {
+    if (fp8w) return FFN_B200_ERR_NOT_APPLICABLE;
+    return plan_rowblock(*pr, grid, out);
+  }
   if (pr->tile_variant > 0 && kVariants[pr->tile_variant - 1].rowblock) return FFN_B200_ERR_INVALID;
+  if (pr->tile_variant > 0 && kVariants[pr->tile_variant - 1].w8 != fp8w) return FFN_B200_ERR_INVALID;
+  // fp8 weights are widened on chip by the decode tiles only (the weight-streaming,
+  // HBM-bound regime where halving the weight bytes matters).
+  if (fp8w && pr->tile_variant == 0 && pr->m > 64) return FFN_B200_ERR_NOT_APPLICABLE;
+  if (fp8w && ((pr->k & 1) || (pr->h & 1))) return FFN_B200_ERR_NOT_APPLICABLE;  // code pairs per TMA element
   int variant;
   if (pr->tile_variant > 0) {
     variant = pr->tile_variant - 1;
     if (kVariants[variant].swap && pr->m > kVariants[variant].bn) return FFN_B200_ERR_INVALID;
     if (kVariants[variant].pair && grid < 2) return FFN_B200_ERR_INVALID;
+  } else if (fp8w) {
+    variant = pr->m <= 16 ? 10 : 11;
   } else if (pr->m <= 16) {
     variant = 2;
   } else if (pr->m <= 64) {
@@ -407,6 +450,13 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   const int64_t pitches[] = {b->ldx, b->ldw1, b->ldw2, rowblock ? b->ldy : b->ldh, b->ldy};
   for (int64_t p : pitches)
     if (p <= 0 || (p % 8) != 0) return FFN_B200_ERR_ALIGNMENT;
+  const bool w8 = kVariants[plan.variant].w8;
+  if (w8) {  // fp8 codes: 1-byte elements, so 16-byte pitches are multiples of 16 elements
+    if ((b->ldw1 % 16) != 0 || (b->ldw2 % 16) != 0) return FFN_B200_ERR_ALIGNMENT;
+    if (!b->w1_scale || !b->w2_scale) return FFN_B200_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(b->w1_scale) & 3u) || (reinterpret_cast<uintptr_t>(b->w2_scale) & 3u))
+      return FFN_B200_ERR_ALIGNMENT;
+  }
   if (b->ldx < prob.k || b->ldw1 < prob.k || b->ldw2 < prob.h || (!rowblock && b->ldh < prob.h) || b->ldy < prob.n)
     return FFN_B200_ERR_INVALID;
 
@@ -443,6 +493,16 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     if (!rc) rc = encode_2d(&P.tm_b_dn, b->w2, dt, prob.h, prob.n, b->ldw2, 64, bn);
     if (!rc) rc = encode_2d(&P.tm_st_hid, b->hidden, dt, prob.h, prob.m, b->ldh, 64, ffnb200::kStoreRows);
     if (!rc) rc = encode_2d(&P.tm_st_y, b->y, dt, prob.n, prob.m, b->ldy, 64, ffnb200::kStoreRows);
+  } else if (w8) {
+    // fp8 weight k-blocks: 128 rows x 64 one-byte codes, 64-byte swizzle (the converter
+    // warps read them bank-conflict free); the token operands as in the 16-bit decode tiles.
+    const uint32_t wbox = static_cast<uint32_t>(64 * kVariants[plan.variant].ksub);  // bytes of a weight row per load
+    rc = encode_2d_u8(&P.tm_a_up, b->w1, prob.k, prob.h, b->ldw1, wbox, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_up, b->x, dt, prob.k, prob.m, b->ldx, 64, bn);
+    if (!rc) rc = encode_2d_u8(&P.tm_a_dn, b->w2, prob.h, prob.n, b->ldw2, wbox, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_dn, b->hidden, dt, prob.h, prob.m, b->ldh, 64, bn);
+    P.w1_scale = b->w1_scale;
+    P.w2_scale = b->w2_scale;
   } else {
     rc = encode_2d(&P.tm_a_up, b->w1, dt, prob.k, prob.h, b->ldw1, 64, 128);
     if (!rc) rc = encode_2d(&P.tm_b_up, b->x, dt, prob.k, prob.m, b->ldx, 64, bn);

@@ -87,6 +87,8 @@ struct Params {
                                // launch adds exactly dp + C (one failed claim per owner)
   int dyn;                     // 1: data-parallel tiles are claimed from `claims` in raster order;
                                // 0: owner c takes tiles c, c + C, ...
+  const float* w1_scale;       // fp8 weights: per-row fp32 scales of W1 [H] and W2 [N]
+  const float* w2_scale;
   // Fused reduce-scatter of the down phase across `rs_world` GPUs (tensor parallel over H):
   // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
   // of another rank's band is pushed as a bf16 partial into that rank's staging buffer over
@@ -247,6 +249,16 @@ __device__ __forceinline__ void umma_f16(uint32_t d, uint64_t a, uint64_t b, uin
       ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
+// Same with the A operand in tensor memory (lane i = row i, two 16-bit K values per
+// 32-bit column; K = 16 spans 8 columns).
+__device__ __forceinline__ void umma_f16_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n"
+      ::"r"(d), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
 // Arrive on an mbarrier once every tcgen05 op issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -357,6 +369,20 @@ __device__ __forceinline__ void umma_commit_pair_both(uint32_t bar) {
 
 // 32 lanes x 32 consecutive 32-bit columns; the wait is in the same asm block so the
 // outputs are never consumed before the load has landed.
+// 32 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers; returns after
+// the stores are complete (tcgen05.wait::st).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t r[32];
   asm volatile(
@@ -504,6 +530,20 @@ __device__ __forceinline__ void gelu2(float& a, float& b) {
     a = gelu_erf(a);
     b = gelu_erf(b);
   }
+}
+// Two e4m3 codes (low byte: the lower-addressed element) -> two fp16 (exact) or bf16 (exact:
+// every e4m3 value is a normal fp16 and a bf16) in one 32-bit word, low half first.
+template <bool BF16>
+__device__ __forceinline__ uint32_t e4m3x2_to_16x2(uint32_t two) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(static_cast<unsigned short>(two & 0xFFFFu)));
+  if constexpr (BF16) {
+    const __half2 hh = *reinterpret_cast<const __half2*>(&h);
+    const float2 f = __half22float2(hh);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+    return *reinterpret_cast<const uint32_t*>(&b);
+  }
+  return h;
 }
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -665,30 +705,59 @@ __device__ __forceinline__ bool wait_word_ge(const unsigned* word, unsigned targ
 // ------------------------------------------------------------------------------------------
 // The kernel
 // ------------------------------------------------------------------------------------------
-template <int BN, int STAGES, bool SWAP, bool PAIR = false, int KSUB = 1, int EPI = 4>
+template <int BN, int STAGES, bool SWAP, bool PAIR = false, int KSUB = 1, int EPI = 4, bool W8 = false>
 struct Layout {
   static constexpr int kEpiWarps = EPI;             // 4, or 8 = two warps per TMEM sub-partition
-  static constexpr int kThreads = kCtrlThreads + 32 * EPI;
+  // fp8 -> 16-bit weight converters: kCvtGroups groups of 4 warps (one per SMSP) take the
+  // k-blocks in turn, so that many k-blocks are in conversion at once.
+  static constexpr int kCvtGroups = W8 ? 3 : 0;
+  static constexpr int kCvtWarps = 4 * kCvtGroups;
+  static constexpr int kThreads = kCtrlThreads + 32 * (EPI + kCvtWarps);
+  static constexpr int kQStage = W8 ? KSUB * kBM * kBK : 0;  // one fp8 weight k-block (128 rows x 64*KSUB bytes)
   static constexpr int kNcta = PAIR ? 2 : 1;       // CTAs per tile (cluster size)
   static constexpr int kBRows = BN / kNcta;         // B rows each CTA loads per stage
   static constexpr int kBSub = kBRows * kBK * 2;    // one 64-wide K sub-block of B
   static constexpr int kAStage = KSUB * kABytes;    // a stage holds KSUB adjacent K sub-blocks
   static constexpr int kBStage = KSUB * kBSub;
-  static constexpr int kStageBytes = kAStage + kBStage;
+  // W8: the widened weight tiles (A) live in TMEM and B in its own ring: no smem stages.
+  static constexpr int kStageBytes = W8 ? 0 : kAStage + kBStage;
   static constexpr int kEpiBytes = SWAP ? 0 : EPI * 2 * kStageBufBytes;
-  static constexpr int kBarBytes = 256;
+  static constexpr int kBarBytes = W8 ? 1024 : 256;
   // Unit ring: the leader's producer publishes each unit it takes (a claimed or static tile)
   // for the MMA issuer, the epilogue warps and, in a pair, the peer CTA.  Deep enough that
   // the producer (at most STAGES k-blocks ahead of the MMA, which is at most two
   // accumulators ahead of the epilogue) never waits on it in steady state.
   static constexpr int kRing = 16;
   static constexpr int kRingBytes = kRing * 32 + 2 * kRing * 8;  // slots, full and empty barriers
-  static constexpr int kRingConsumers = PAIR ? 2 + 2 * EPI : 1 + EPI;  // MMA + epilogue warps (+ peer's producer and epilogue)
-  static constexpr int kSmem = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiBytes + kBarBytes + kRingBytes;
+  // MMA + epilogue warps (+ peer's producer and epilogue, + converter warps)
+  static constexpr int kRingConsumers = (PAIR ? 2 + 2 * EPI : 1 + EPI) + kCvtWarps;
+  // W8: a ring of fp8 weight k-blocks deeper than the MMA stages (the bytes in flight set the
+  // HBM rate of the weight stream), 1024-aligned after the barriers and the unit ring.
+  // The token operand (B) then has its own ring of the same depth, read by the MMA in place,
+  // so the MMA stages hold only the widened weights and no memory latency sits in their cycle.
+  // (a converter's slot waits stay unambiguous while kQSlots >= STAGES + kCvtGroups + 1)
+  static constexpr int kQSlots = W8 ? (BN <= 16 ? 10 : 9) : 0;
+  static constexpr int kBSlots = W8 ? (BN <= 16 ? 10 : 4) : 0;  // (one producer, one in-order consumer)
+  static constexpr int kQOffset = (kBarBytes + kRingBytes + 1023) / 1024 * 1024;  // from the barrier area
+  static constexpr int kBRingOffset = kQOffset + kQSlots * kQStage;
+  static constexpr int kSmem = 1024 /*align slack*/ + STAGES * kStageBytes + kEpiBytes +
+                               (W8 ? kBRingOffset + kBSlots * kBStage : kBarBytes + kRingBytes);
   static_assert(kSmem <= 232448, "dynamic shared memory per CTA");
-  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  // W8: two accumulators then STAGES weight tiles of 32 columns (128 rows x 64 16-bit K).
+  // Decode (swap-AB) tiles have N = 16 or 64: one MMA does little work, and MMAs that add
+  // into the same accumulator run one after the other, so their latency, not the tensor
+  // pipe, would set the pace.  K-step i therefore adds into chain i mod kChains, an
+  // accumulator of its own; the epilogue sums the chains in a fixed order.
+  static constexpr int kChains = SWAP ? (BN <= 16 ? 4 : 2) : 1;
+  static constexpr int kAccCols = kChains * BN;  // one accumulator buffer
+  static constexpr int kTmemCols = W8 ? 512 : (2 * kAccCols < 32 ? 32 : 2 * kAccCols);
+  static constexpr int kTmemA = 32 * KSUB;  // W8: TMEM columns of one widened weight k-block
+  static_assert(!W8 || 2 * kAccCols + kTmemA * STAGES <= 512, "TMEM: accumulators and weight stages");
+  static_assert(kChains <= 4 * KSUB, "every chain gets a K step from each k-block");
+  static_assert(!W8 || (kQSlots >= STAGES + kCvtGroups + 1 && kCvtGroups <= STAGES), "ring depths");
   static_assert((kBSub % 1024) == 0, "B tile must be whole swizzle atoms");
-  static_assert((2 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");
+  static_assert((W8 ? 2 * STAGES + 6 + 2 * kQSlots + 2 * kBSlots : 2 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");
+  static_assert(!W8 || (SWAP && !PAIR && (KSUB == 1 || KSUB == 2)), "fp8 weights: swap-AB decode tiles");
   static_assert(!PAIR || !SWAP, "CTA pairs are used for prefill tiles only");
   static_assert(EPI == 4 || EPI == 8, "epilogue warps: one or two per TMEM sub-partition");
 };
@@ -699,9 +768,10 @@ struct Layout {
 // barrier; the leader's MMA thread issues the pair MMAs, whose D lands 128 rows in each
 // CTA's TMEM, and its tcgen05.commit arrives on the empty / tmem-full barriers of both CTAs;
 // each CTA's epilogue stores its own 128 rows and releases the accumulator on the leader.
-template <int BN, int STAGES, bool SWAP, bool PAIR, int KSUB, int EPI, bool BF16, int GELU>
-__global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(const __grid_constant__ Params p) {
-  using LY = Layout<BN, STAGES, SWAP, PAIR, KSUB, EPI>;
+template <int BN, int STAGES, bool SWAP, bool PAIR, int KSUB, int EPI, bool BF16, int GELU, bool W8 = false>
+__global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
+    ffn_fused_kernel(const __grid_constant__ Params p) {
+  using LY = Layout<BN, STAGES, SWAP, PAIR, KSUB, EPI, W8>;
   constexpr int kParts = EPI / 4;  // epilogue warps per TMEM sub-partition, each takes a column share
   // Swap mode reads TMEM in chunks of kCW token columns; normal mode in 64-column chunks.
   constexpr int kCW = SWAP ? (BN / kParts < 16 ? BN / kParts : 16) : 64;
@@ -709,7 +779,10 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
   static_assert(kChunks % kParts == 0, "column chunks split evenly over the warps of a sub-partition");
   constexpr int kNcta = LY::kNcta;
   constexpr int kTileM = kBM * kNcta;
-  constexpr uint32_t kIdesc = make_idesc<BF16, BN, kTileM>();
+  // W8 multiplies fp16 x fp16: the widened weights are exact in fp16 and the token tiles
+  // (16-bit activations) are moved to fp16 in shared memory (bf16 -> fp16 is exact inside
+  // fp16's range; a value beyond it is reported as kernel error 6).
+  constexpr uint32_t kIdesc = make_idesc<BF16 && !W8, BN, kTileM>();
   static_assert(SWAP || (BN % 64) == 0, "normal mode stores 64-column chunks");
   static_assert(!SWAP || (BN % 16) == 0, "swap mode loads 16-column chunks");
 
@@ -719,7 +792,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t sA = base;
   const uint32_t sB = sA + STAGES * LY::kAStage;
-  const uint32_t sE = sB + STAGES * LY::kBStage;
+  const uint32_t sE = W8 ? sA : sB + STAGES * LY::kBStage;  // (W8: no smem stages)
   const uint32_t sBar = sE + LY::kEpiBytes;
   auto full_bar = [&](int s) { return sBar + 8u * s; };
   auto empty_bar = [&](int s) { return sBar + 8u * (STAGES + s); };
@@ -729,6 +802,12 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (sBar - base) + 8 * (2 * STAGES + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t sRing = sBar + LY::kBarBytes;
+  const uint32_t sQ = sBar + LY::kQOffset;      // fp8 weight k-blocks (W8), 1024-aligned
+  const uint32_t sBR = sBar + LY::kBRingOffset;  // token-operand k-blocks (W8), 1024-aligned
+  auto qfull_bar = [&](int j) { return sBar + 8u * (2 * STAGES + 6 + j); };
+  auto qempty_bar = [&](int j) { return sBar + 8u * (2 * STAGES + 6 + LY::kQSlots + j); };
+  auto bfull_bar = [&](int j) { return sBar + 8u * (2 * STAGES + 6 + 2 * LY::kQSlots + j); };
+  auto bempty_bar = [&](int j) { return sBar + 8u * (2 * STAGES + 6 + 2 * LY::kQSlots + LY::kBSlots + j); };
   auto ring_slot = [&](int i) { return sRing + 32u * i; };
   auto ring_full = [&](int i) { return sRing + 32u * LY::kRing + 8u * i; };
   auto ring_empty = [&](int i) { return sRing + 32u * LY::kRing + 8u * (LY::kRing + i); };
@@ -744,8 +823,21 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
   if (threadIdx.x == 0) {
 #pragma unroll 1
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full_bar(s), 1);
+      // W8: one arrival per warp of the converter group that owns the k-block.
+      mbar_init(full_bar(s), W8 ? 4 : 1);
       mbar_init(empty_bar(s), 1);
+    }
+    if constexpr (W8) {
+#pragma unroll 1
+      for (int j = 0; j < LY::kQSlots; ++j) {
+        mbar_init(qfull_bar(j), 1);
+        mbar_init(qempty_bar(j), 4);
+      }
+#pragma unroll 1
+      for (int j = 0; j < LY::kBSlots; ++j) {
+        mbar_init(bfull_bar(j), 1);
+        mbar_init(bempty_bar(j), 1);
+      }
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
@@ -808,6 +900,37 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
         unit_coords(p, u, tr, tq);
         const CUtensorMap* ta = u.phase ? &p.tm_a_dn : &p.tm_a_up;
         const CUtensorMap* tb = u.phase ? &p.tm_b_dn : &p.tm_b_up;
+        if constexpr (W8) {
+          // K-block n: fp8 weights to q slot n mod Q (for the converters), tokens to B slot
+          // n mod QB (read by the MMA in place), ahead of the MMA by up to the ring depths.  A
+          // down unit's tokens (hidden rows) wait for the rows to be ready; its weights never
+          // wait.  One k-block is KSUB x 64 K: 64*KSUB bytes of each weight row per load.
+          const int wrow = tr * kTileM;
+#pragma unroll 1
+          for (int kb = u.kb0; kb < u.kb1; ++kb) {
+            const int j = static_cast<int>(issued % LY::kQSlots);
+            const uint32_t rpar = static_cast<uint32_t>((issued / LY::kQSlots) & 1);
+            if (!wait_bar(qempty_bar(j), rpar ^ 1u, abort_flag, p, 150 + j)) return false;
+            mbar_expect_tx(qfull_bar(j), LY::kQStage);
+            tma_load_2d(sQ + j * LY::kQStage, ta, kb * kBK * KSUB / 2, wrow, qfull_bar(j));  // (code pairs)
+            const int jb = static_cast<int>(issued % LY::kBSlots);
+            const uint32_t bpar = static_cast<uint32_t>((issued / LY::kBSlots) & 1);
+            if (!wait_bar(bempty_bar(jb), bpar ^ 1u, abort_flag, p, 170 + jb)) return false;
+            if (u.phase == 1 && tq != ready_blk) {  // swap mode: the row block is a token block
+              if (!wait_word_ge(p.counters + tq, target, abort_flag, p, 2, tq)) return false;
+              fence_async_global();
+              if (ready_blk < 0) trace_mark(p, kTrDownReady);
+              ready_blk = tq;
+            }
+            mbar_expect_tx(bfull_bar(jb), LY::kBStage);
+#pragma unroll
+            for (int jj = 0; jj < KSUB; ++jj)
+              tma_load_2d(sBR + jb * LY::kBStage + jj * LY::kBSub, tb, (kb * KSUB + jj) * kBK, tq * BN, bfull_bar(jb));
+            if (issued == 0) trace_mark(p, kTrFirstLoad);
+            ++issued;
+          }
+          return true;
+        }
         const int arow = tr * kTileM + static_cast<int>(rank) * kBM;
         const int brow = tq * BN + static_cast<int>(rank) * LY::kBRows;
         // One operand load into stage `st` (which = 0: A, 1: B), with the chosen L2 policy.
@@ -972,17 +1095,34 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
       // transaction bytes land on the leader's barriers, so the leader drains for both.
       // One deadline for the whole drain: after an abort, stages armed for both operands
       // but given only the weight operand never complete, and must not each wait the limit.
+      if constexpr (W8) {  // the token loads of the last kBSlots k-blocks land too
+        const long long firstb = issued > LY::kBSlots ? issued - LY::kBSlots : 0;
+        const uint64_t tb0 = gtimer();
+#pragma unroll 1
+        for (long long i = firstb; i < issued; ++i) {
+          const int jb = static_cast<int>(i % LY::kBSlots);
+          const uint32_t par = static_cast<uint32_t>((i / LY::kBSlots) & 1);
+          bool late = false;
+          while (!mbar_try_wait(bfull_bar(jb), par)) {
+            if (gtimer() - tb0 > p.wait_limit_ns) { late = true; break; }
+          }
+          if (late) break;
+        }
+      }
       if (leader) {
-        const long long first = issued > STAGES ? issued - STAGES : 0;
+        // (W8: the producer's own loads are the fp8 k-blocks of the q ring.)
+        constexpr int kRingDepth = W8 ? LY::kQSlots : STAGES;
+        const long long first = issued > kRingDepth ? issued - kRingDepth : 0;
         const uint64_t t0 = gtimer();
         bool late = false;
 #pragma unroll 1
         for (long long i = first; i < issued && !late; ++i) {
-          const int s = static_cast<int>(i % STAGES);
-          const uint32_t par = static_cast<uint32_t>((i / STAGES) & 1);
-          while (!mbar_try_wait(full_bar(s), par)) {
+          const int s = static_cast<int>(i % kRingDepth);
+          const uint32_t par = static_cast<uint32_t>((i / kRingDepth) & 1);
+          while (!mbar_try_wait(W8 ? qfull_bar(s) : full_bar(s), par)) {
             if (gtimer() - t0 > p.wait_limit_ns) { late = true; break; }
           }
+
         }
       }
     }
@@ -993,6 +1133,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      long long kn = 0;  // W8: k-blocks consumed (token-operand ring position)
       bool ok = true;
 #pragma unroll 1
       for (int seq = 0; ok; ++seq) {
@@ -1008,27 +1149,42 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
         unpack_unit(w, u);
         if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, p, 200 + acc)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * LY::kAccCols);
 #pragma unroll 1
         for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!wait_bar(full_bar(stage), phase, abort_flag, p, 300 + stage)) { ok = false; break; }
+          uint32_t sbk = sB + stage * LY::kBStage;  // this k-block's B tile
+          int bslot = 0;
+          if constexpr (W8) {  // the token tile waits in its own ring slot
+            bslot = static_cast<int>(kn % LY::kBSlots);
+            const uint32_t bpar = static_cast<uint32_t>((kn / LY::kBSlots) & 1);
+            if (!wait_bar(bfull_bar(bslot), bpar, abort_flag, p, 320 + bslot)) { ok = false; break; }
+            sbk = sBR + bslot * LY::kBStage;
+            ++kn;
+          }
           tc_fence_after();
 #pragma unroll
           for (int j = 0; j < KSUB; ++j) {
             const uint64_t da = sw128_desc(sA + stage * LY::kAStage + j * kABytes);
-            const uint64_t db = sw128_desc(sB + stage * LY::kBStage + j * LY::kBSub);
+            const uint64_t db = sw128_desc(sbk + j * LY::kBSub);
+            const uint32_t ta =
+                tmem_base + static_cast<uint32_t>(2 * LY::kAccCols + LY::kTmemA * stage + 32 * j);  // W8: A in TMEM
 #pragma unroll
             for (int k = 0; k < kBK / 16; ++k) {
               // +32 bytes along K inside the 128-byte swizzle atom = +2 in the 16-byte address field
-              const uint32_t accum = (kb > u.kb0 || j > 0 || k > 0) ? 1u : 0u;
-              if constexpr (PAIR) umma_f16_pair(d, da + 2 * k, db + 2 * k, kIdesc, accum);
-              else umma_f16(d, da + 2 * k, db + 2 * k, kIdesc, accum);
+              const int ks = (j * (kBK / 16) + k);  // K step within the k-block
+              const uint32_t dc = d + static_cast<uint32_t>((ks % LY::kChains) * BN);
+              const uint32_t accum = (kb > u.kb0 || ks >= LY::kChains) ? 1u : 0u;
+              if constexpr (PAIR) umma_f16_pair(dc, da + 2 * k, db + 2 * k, kIdesc, accum);
+              else if constexpr (W8) umma_f16_ta(dc, ta + 8 * k, db + 2 * k, kIdesc, accum);
+              else umma_f16(dc, da + 2 * k, db + 2 * k, kIdesc, accum);
             }
           }
           if constexpr (PAIR) {
             umma_commit_pair_both(empty_bar(stage));
           } else {
             umma_commit(empty_bar(stage));
+            if constexpr (W8) umma_commit(bempty_bar(bslot));
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -1047,6 +1203,114 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
       const uint64_t t0 = gtimer();
       while (!mbar_try_wait(drain_bar, 0)) {
         if (gtimer() - t0 > p.wait_limit_ns) break;
+      }
+    }
+  } else if (warp >= kCtrlThreads / 32 + EPI) {
+    // ---------------------------------------------------------------- fp8 weight converters (W8)
+    // Group g takes k-blocks g, g + G, g + 2G, ... of the CTA's sequence (k-block n: q slot
+    // n mod Q, MMA stage n mod STAGES).  For each, its 4 warps wait for the fp8 k-block; each
+    // warp widens the 64 fp8 codes of the 32 weight rows of its TMEM sub-partition to the
+    // problem's 16-bit type, frees the q slot, waits for the stage's TMEM columns to be free
+    // and stores the rows there (the MMA's A operand in tensor memory), then arrives.
+    if constexpr (W8) {
+      const int cw = warp - (kCtrlThreads / 32 + EPI);
+      const int group = cw >> 2;
+      const int r = (warp & 3) * 32 + lane;  // row of the A tile = TMEM lane of this warp
+      const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+      long long n = 0;  // k-blocks of this CTA seen so far
+      int ok = 1;
+#pragma unroll 1
+      for (int seq = 0; ok; ++seq) {
+        const int slot = seq % LY::kRing;
+        const uint32_t rpar = static_cast<uint32_t>((seq / LY::kRing) & 1);
+        if (lane == 0) ok = wait_bar(ring_full(slot), rpar, abort_flag, p, 600 + slot) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane != 0) (void)mbar_try_wait(ring_full(slot), rpar);
+        int w[8];
+        ld_shared_8(ring_slot(slot), w);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ring_empty(slot));
+        if (!w[7]) break;
+        const int nkb = w[3] - w[2];
+#pragma unroll 1
+        for (int i = 0; i < nkb; ++i, ++n) {
+          if (n % LY::kCvtGroups != group) continue;  // another group's k-block
+          const int j = static_cast<int>(n % LY::kQSlots);
+          const uint32_t qpar = static_cast<uint32_t>((n / LY::kQSlots) & 1);
+          const int st = static_cast<int>(n % STAGES);
+          const uint32_t spar = static_cast<uint32_t>((n / STAGES) & 1);
+          if (lane == 0) ok = wait_bar(qfull_bar(j), qpar, abort_flag, p, 700 + j) ? 1 : 0;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          if (lane != 0) (void)mbar_try_wait(qfull_bar(j), qpar);
+          // Row r of the q slot: 64*KSUB codes.  The box carries the TMA's swizzle: with
+          // 64-byte rows (KSUB 1) 16-byte chunk c sits at c ^ ((r >> 1) & 3), with 128-byte rows
+          // (KSUB 2) at c ^ (r & 7); either way 8 consecutive rows cover all banks.
+          const uint32_t src = sQ + static_cast<uint32_t>(j * LY::kQStage + r * 64 * KSUB);
+          uint32_t q[16 * KSUB];
+#pragma unroll
+          for (int c = 0; c < 4 * KSUB; ++c) {
+            const int pc = KSUB == 2 ? (c ^ (r & 7)) : (c ^ ((r >> 1) & 3));
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(q[4 * c]), "=r"(q[4 * c + 1]), "=r"(q[4 * c + 2]), "=r"(q[4 * c + 3])
+                         : "r"(src + (pc << 4))
+                         : "memory");
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(qempty_bar(j));  // the codes are in registers
+          if constexpr (BF16) {
+            // The token tile of this k-block (B ring slot n mod QB, landed by TMA): bf16 ->
+            // fp16 in place, 128B-swizzled positions unchanged.  The 4 warps of the group split
+            // it; each thread converts 8-element (16-byte) pieces.
+            const int jb = static_cast<int>(n % LY::kBSlots);
+            const uint32_t bpar = static_cast<uint32_t>((n / LY::kBSlots) & 1);
+            if (lane == 0) ok = wait_bar(bfull_bar(jb), bpar, abort_flag, p, 720 + jb) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            if (lane != 0) (void)mbar_try_wait(bfull_bar(jb), bpar);
+            constexpr int kPieces = LY::kBStage / 16;  // 16-byte pieces of the tile
+            const uint32_t bbase = sBR + static_cast<uint32_t>(jb * LY::kBStage);
+            bool range_ok = true;
+#pragma unroll 1
+            for (int piece = (warp & 3) * 32 + lane; piece < kPieces; piece += 128) {
+              uint32_t v[4];
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                           : "r"(bbase + piece * 16)
+                           : "memory");
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float lo = __uint_as_float(v[e] << 16), hi = __uint_as_float(v[e] & 0xFFFF0000u);
+                range_ok = range_ok && fabsf(lo) <= 65504.0f && fabsf(hi) <= 65504.0f;
+                const __half2 h = __floats2half2_rn(lo, hi);
+                v[e] = *reinterpret_cast<const uint32_t*>(&h);
+              }
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(bbase + piece * 16), "r"(v[0]), "r"(v[1]),
+                           "r"(v[2]), "r"(v[3])
+                           : "memory");
+            }
+            if (!range_ok) report(p, 6, static_cast<int>(n));  // recorded, the results are not valid
+            fence_async_shared();
+          }
+          if (lane == 0) ok = wait_bar(empty_bar(st), spar ^ 1u, abort_flag, p, 100 + st) ? 1 : 0;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          tc_fence_after();  // the MMAs that read these columns have completed
+#pragma unroll
+          for (int jj = 0; jj < KSUB; ++jj) {
+            uint32_t o[32];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              o[2 * k] = e4m3x2_to_16x2<false>(q[16 * jj + k]);
+              o[2 * k + 1] = e4m3x2_to_16x2<false>(q[16 * jj + k] >> 16);
+            }
+            tmem_st32(tmem_base + lane_off + static_cast<uint32_t>(2 * LY::kAccCols + LY::kTmemA * st + 32 * jj), o);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(full_bar(st));
+        }
       }
     }
   } else {
@@ -1105,7 +1369,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
         for (int c2 = u.c_first; c2 <= u.c_last; ++c2)
           (void)ld_acquire(p.flags + (u.phase * p.C + c2) * kNcta + slot_base);
       }
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * LY::kAccCols);
       auto ws_row = [&](int c) {
         return p.ws + (static_cast<size_t>((u.phase * p.C + c) * kNcta + slot_base) * kBM + row) * BN;
       };
@@ -1246,6 +1511,14 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
           float v[kCW];
           if constexpr (kCW == 16) tmem_ld16(tbase + ch * kCW, v);
           else tmem_ld8(tbase + ch * kCW, v);
+#pragma unroll
+          for (int c = 1; c < LY::kChains; ++c) {  // the other K chains, in order
+            float w[kCW];
+            if constexpr (kCW == 16) tmem_ld16(tbase + c * BN + ch * kCW, w);
+            else tmem_ld8(tbase + c * BN + ch * kCW, w);
+#pragma unroll
+            for (int j = 0; j < kCW; ++j) v[j] += w[j];
+          }
           if (u.role == kRoleContrib) {
             float4* dst = reinterpret_cast<float4*>(ws_own + ch * kCW);
 #pragma unroll
@@ -1261,6 +1534,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * EPI, 1) ffn_fused_kernel(c
                 const float4 t = __ldcg(src + j);
                 v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
               }
+            }
+          }
+          if constexpr (W8) {  // fp8 weights: the row's scale factors out of the K sum
+            if (feat < F) {
+              const float sc = __ldg((u.phase ? p.w2_scale : p.w1_scale) + feat);
+#pragma unroll
+              for (int j = 0; j < kCW; ++j) v[j] *= sc;
             }
           }
           if (feat < F) {

@@ -98,6 +98,31 @@ def _packed(t, rows, cols):
     return buf
 
 
+def quantize_weights_fp8(weight):
+    """fp8 weights for the decode tiles: ``weight`` [rows, cols] (fp16/bf16, CUDA) becomes
+    ``(codes, scales)``: uint8 e4m3 codes [rows, pitch] (pitch = cols rounded up to 16
+    bytes, the TMA rule for 1-byte elements) and fp32 row scales [rows], with
+    ``weight[r, c] ~= e4m3(codes[r, c]) * scales[r]`` (per-row absmax / 448, RN-even,
+    saturating; computed on the device by ``ffn_b200_quantize_fp8_rows``)."""
+    import ctypes
+
+    import torch
+
+    from .. import _lib
+
+    rows, cols = weight.shape
+    src = weight if _tma_ready(weight, rows, cols) else _packed(weight.contiguous(), rows, cols)
+    codes = torch.zeros((rows, (cols + 15) // 16 * 16), dtype=torch.uint8, device=weight.device)
+    scales = torch.empty(rows, dtype=torch.float32, device=weight.device)
+    dtype = str(weight.dtype).removeprefix("torch.")
+    rc = _lib.load().ffn_b200_quantize_fp8_rows(src.data_ptr(), src.stride(0), _lib.DTYPES[dtype], rows, cols,
+                                                codes.data_ptr(), codes.stride(0), scales.data_ptr(),
+                                                ctypes.c_void_p(torch.cuda.current_stream(weight.device).cuda_stream))
+    if rc != _lib.OK:
+        raise ValueError(f"ffn_b200_quantize_fp8_rows: {_lib.strerror(rc)}")
+    return codes, scales
+
+
 def prepare_storage(x, weight1, weight2, plan):
     """Device storage for one prepared FFN (reference ops/host/inputs.py:74-90).
 
@@ -117,6 +142,7 @@ def prepare_storage(x, weight1, weight2, plan):
     dev = x.device
     xs = x.reshape(p.m, p.k) if x.is_contiguous() else x.contiguous().view(p.m, p.k)
     x2d = _packed(xs, p.m, p.k)
+    # (fp8 weights arrive here as uint8 code views with 16-byte pitches: used in place)
     w1 = weight1 if _tma_ready(weight1, p.h, p.k) else _packed(weight1.contiguous(), p.h, p.k)
     w2 = weight2 if _tma_ready(weight2, p.n, p.h) else _packed(weight2.contiguous(), p.n, p.h)
     # full_load_a keeps the hidden row block on chip: an 8-column stand-in keeps the

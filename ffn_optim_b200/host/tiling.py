@@ -91,7 +91,7 @@ def device_sm_count(device=None):
 
 
 def problem_struct(problem, down_impl, gelu, block_num, sms, tile=None, raster_group=None, l2_policy=None,
-                   schedule=None):
+                   schedule=None, weight_format=None):
     """The C ABI's ffn_b200_problem for a validated Problem and the tuning overrides."""
     from .. import _lib
 
@@ -99,18 +99,20 @@ def problem_struct(problem, down_impl, gelu, block_num, sms, tile=None, raster_g
                         _lib.DOWN_IMPL_CODES[down_impl], _lib.GELU_CODES[gelu], block_num, sms,
                         _lib.TILE_VARIANTS[tile] if tile else 0, int(raster_group or 0),
                         _lib.L2_POLICIES[l2_policy] if l2_policy else 0,
-                        _lib.SCHEDULES[schedule] if schedule else 0)
+                        _lib.SCHEDULES[schedule] if schedule else 0,
+                        _lib.WEIGHT_FORMATS[weight_format] if weight_format else 0)
 
 
 def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational", sm_count=None, tile=None,
-              raster_group=None, l2_policy=None, schedule=None):
+              raster_group=None, l2_policy=None, schedule=None, weight_format=None):
     """Plans one fused launch (reference ops/host/tiling.py:58-74).
 
     ``block_num`` None means one CTA per SM.  ``tile`` None picks the kernel variant
     automatically; a name of ``_lib.TILE_VARIANTS`` forces one (tests, benchmarks).
     ``raster_group`` (tile rows per raster group), ``l2_policy`` ('none' | 'stream_b' | ...)
     and ``schedule`` ('static' | 'dynamic' data-parallel tile order) override the
-    automatic tuning.  Raises
+    automatic tuning; ``weight_format='fp8'`` plans the fp8-weight decode tiles (M <= 64,
+    otherwise NotApplicable).  Raises
     DependencyUnavailable for the full-load variants, NotApplicable for Stream-K without a
     tail wave (the reference's rule, applied to this kernel's tile grid), ValueError
     otherwise.
@@ -133,11 +135,16 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
         raise ValueError("raster_group must be a positive integer")
     if schedule is not None and schedule not in _lib.SCHEDULES:
         raise ValueError(f"schedule must be None or one of {sorted(_lib.SCHEDULES)}")
+    if weight_format is not None and weight_format not in _lib.WEIGHT_FORMATS:
+        raise ValueError(f"weight_format must be None or one of {sorted(_lib.WEIGHT_FORMATS)}")
     lib = _lib.load()
-    prob = problem_struct(problem, selection.down_impl, gelu, block_num, sms, tile, raster_group, l2_policy, schedule)
+    prob = problem_struct(problem, selection.down_impl, gelu, block_num, sms, tile, raster_group, l2_policy, schedule,
+                          weight_format)
     info = _lib.PlanInfo()
     rc = lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info))
     if rc == _lib.ERR_NOT_APPLICABLE:
+        if weight_format == "fp8":
+            raise NotApplicable("fp8 weights: decode tiles only (M <= 64, even K and H, down_impl basic or streamk)")
         if selection.down_impl == "full_load_a":
             raise NotApplicable("full_load_a keeps a 128 x N fp32 row block in TMEM: needs N <= 256")
         raise NotApplicable("Stream-K candidate has no remainder tiles for this block_num "
@@ -150,5 +157,6 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
     up = Tile(info.tile_m, info.tile_n, info.tile_k, info.stages)
     down = Tile(info.tile_m, info.tile_n, info.tile_k, info.stages)
     ws_shape = (2 * info.block_num * 128, info.tile_n)
-    kernel["overrides"] = {"tile": tile, "raster_group": raster_group, "l2_policy": l2_policy, "schedule": schedule}
+    kernel["overrides"] = {"tile": tile, "raster_group": raster_group, "l2_policy": l2_policy, "schedule": schedule,
+                           "weight_format": weight_format}
     return Plan(problem, selection, info.block_num, up, down, ws_shape, gelu, kernel)

@@ -66,6 +66,11 @@ typedef enum {
  * ERF calls CUDA's erff. */
 typedef enum { FFN_B200_GELU_RATIONAL = 0, FFN_B200_GELU_ERF = 1 } ffn_b200_gelu;
 
+/* Weight storage: the input dtype, or fp8 e4m3 codes with one fp32 scale per row
+ * (W[r, c] = code[r, c] * scale[r]; see ffn_b200_quantize_fp8_rows).  fp8 weights are
+ * widened to the input dtype on chip; they apply to decode tiles (M <= 64). */
+typedef enum { FFN_B200_WEIGHTS_NATIVE = 0, FFN_B200_WEIGHTS_FP8_ROWS = 1 } ffn_b200_weight_format;
+
 /* Device-side error codes written to status[0] by the kernel (0 = no error). */
 typedef enum {
   FFN_B200_KERNEL_OK = 0,
@@ -73,8 +78,10 @@ typedef enum {
   FFN_B200_KERNEL_DEP_TIMEOUT = 2,  /* a down tile waited too long for its hidden rows */
   FFN_B200_KERNEL_SK_TIMEOUT = 3,   /* a Stream-K owner waited too long for a partial */
   FFN_B200_KERNEL_PEER_TIMEOUT = 4, /* a band owner waited too long for another GPU's partial */
-  FFN_B200_KERNEL_CLAIM_RANGE = 5   /* a tile claim fell outside this launch's range: the
+  FFN_B200_KERNEL_CLAIM_RANGE = 5,  /* a tile claim fell outside this launch's range: the
                                        counters were not reset after an earlier error */
+  FFN_B200_KERNEL_FP16_RANGE = 6    /* fp8 weights with bf16 activations: an activation is
+                                       beyond +-65504, the fp16 range of that path's MMA */
 } ffn_b200_kernel_error;
 
 typedef struct {
@@ -97,6 +104,7 @@ typedef struct {
                            2 dynamic (after its first tile each owner claims the next tile of the
                            raster from a device counter); 0 = dynamic for CTA-pair tiles,
                            static otherwise */
+  int32_t weight_format; /* ffn_b200_weight_format of W1 and W2 */
 } ffn_b200_problem;
 
 /* One GEMM phase (up: Z = X.W1^T, down: Y = hidden.W2^T) as scheduled on the device.
@@ -142,6 +150,8 @@ typedef struct {
   uint32_t* counters;
   uint32_t* flags;
   int32_t* status;
+  const float* w1_scale; /* FFN_B200_WEIGHTS_FP8_ROWS: [H] and [N] fp32 row scales, else NULL */
+  const float* w2_scale;
 } ffn_b200_buffers;
 
 typedef struct ffn_b200_handle ffn_b200_handle;
@@ -224,6 +234,14 @@ FFN_B200_EXPORT int ffn_b200_set_trace(ffn_b200_handle* handle, uint64_t* device
  * or to 0 for launch order.  No reference counterpart (the reference's block-to-tile order
  * is its launch order). */
 FFN_B200_EXPORT int ffn_b200_set_owner_map(ffn_b200_handle* handle, const int32_t* device_map);
+
+/* fp8 weights: row r of `src` [rows, cols] (fp16/bf16, pitch ld_src elements) becomes
+ * scales[r] = absmax(row) / 448 (1 for a zero row) and codes dst[r, c] =
+ * RN-even, saturating e4m3(src[r, c] / scales[r]) with IEEE fp32 division; dst pitch ld_dst
+ * bytes (a multiple of 16 for TMA).  Asynchronous on `stream`.  No reference counterpart
+ * (the reference has no quantized weights). */
+FFN_B200_EXPORT int ffn_b200_quantize_fp8_rows(const void* src, int64_t ld_src, int32_t dtype, int64_t rows,
+                                               int64_t cols, void* dst, int64_t ld_dst, float* scales, void* stream);
 FFN_B200_EXPORT int ffn_b200_get_owner_map(const ffn_b200_handle* handle, int32_t* host_out, int32_t capacity,
                                            int32_t* count);
 

@@ -16,6 +16,12 @@ It restates, in numpy (float32 BLAS + explicit rounding), the reference's torch 
   * :func:`round_to`       <- the ``.to(x.dtype)`` casts: IEEE round-to-nearest-even to fp16 /
     bf16
 
+Beyond the reference (its V1 has no quantized weights): :func:`quantize_rows_e4m3` and
+:func:`ffn_fp8_weights` restate this build's fp8-weight decode path -- per-row scale
+absmax/448 (IEEE fp32 division), codes RN-even with saturation to +-448 in the OCP e4m3
+("fn") format, activations entering the MMA as fp16, the kernel's fp32 sum multiplied by
+the row scale.
+
 Pinning: ``tests/golden/`` holds outputs of the reference's own ``ffn_torch`` (imported from
 the reference checkout by ``tests/golden/make_golden.py``) on the seeded inputs of each case;
 ``tests/test_oracle.py`` checks this restatement against them (at most one unit in the last
@@ -120,3 +126,66 @@ def ulp_distance(a_bits, b_bits):
         b = np.asarray(b, dtype=np.uint16).astype(np.int32)
         return np.where(b & 0x8000, 0x8000 - (b & 0x7FFF), 0x8000 + b)
     return np.abs(key(a_bits) - key(b_bits))
+
+
+def _e4m3_table():
+    """float32 value of every e4m3 code (sign | 4-bit exponent, bias 7 | 3-bit mantissa);
+    0x7F / 0xFF are NaN, there are no infinities."""
+    vals = np.zeros(256, dtype=np.float32)
+    for code in range(256):
+        sign = -1.0 if code & 0x80 else 1.0
+        e, m = (code >> 3) & 0xF, code & 0x7
+        if e == 15 and m == 7:
+            vals[code] = np.nan
+        elif e == 0:
+            vals[code] = sign * (m / 8.0) * 2.0 ** -6
+        else:
+            vals[code] = sign * (1.0 + m / 8.0) * 2.0 ** (e - 7)
+    return vals
+
+
+E4M3_VALUES = _e4m3_table()
+_E4M3_POS = E4M3_VALUES[:127]  # codes 0..126: the finite non-negative values, ascending
+
+
+def e4m3_codes(v):
+    """float32 -> e4m3 codes: round to nearest, ties to the even code, saturate to +-448
+    (the cvt.rn.satfinite.e4m3x2.f32 rule); the sign of zero is kept."""
+    v = np.asarray(v, dtype=np.float32)
+    a = np.minimum(np.abs(v), np.float32(448.0))
+    hi = np.clip(np.searchsorted(_E4M3_POS, a, side="left"), 0, 126)
+    lo = np.maximum(hi - 1, 0)
+    d_lo = a - _E4M3_POS[lo]
+    d_hi = _E4M3_POS[hi] - a
+    pick_hi = (d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo).astype(np.uint8)
+    return np.where(np.signbit(v), code | np.uint8(0x80), code).astype(np.uint8)
+
+
+def quantize_rows_e4m3(w):
+    """Per-row fp8 quantization of ``w`` [rows, cols] (float32 holding fp16/bf16 values):
+    returns (codes uint8 [rows, cols], scales float32 [rows])."""
+    w = np.asarray(w, dtype=np.float32)
+    amax = np.abs(w).max(axis=1)
+    scales = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
+    return e4m3_codes(w / scales[:, None]), scales
+
+
+def _as_fp16(a):
+    """Round-to-nearest-even to fp16 (subnormals kept), back to float32: the fp8-weight
+    path multiplies fp16 x fp16, so 16-bit activations enter the MMA as fp16."""
+    return np.asarray(a, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def ffn_fp8_weights(x, q1, s1, q2, s2, dtype, *, rational=True):
+    """The fp8-weight path on float32 activations: z = (fp16(x) . e4m3(q1)^T) * s1, hidden =
+    RN_dtype(GELU(z)), y = RN_dtype((fp16(hidden) . e4m3(q2)^T) * s2).  (fp16(.) is exact
+    for bf16 values inside fp16's normal range.)  Returns uint16 bits."""
+    x = np.asarray(x, dtype=np.float32)
+    lead = x.shape[:-1]
+    w1 = E4M3_VALUES[np.asarray(q1, dtype=np.uint8)]
+    w2 = E4M3_VALUES[np.asarray(q2, dtype=np.uint8)]
+    z = (_as_fp16(x.reshape(-1, x.shape[-1])) @ w1.T) * np.asarray(s1, dtype=np.float32)
+    hidden = round_to(gelu_rational(z) if rational else gelu_erf(z), dtype)
+    y = (_as_fp16(hidden) @ w2.T) * np.asarray(s2, dtype=np.float32)
+    return to_bits(y, dtype).reshape(*lead, w2.shape[0])

@@ -94,3 +94,43 @@ def test_seeded_inputs_are_deterministic():
     case = C.get_case("cfg1_fp16")
     full = C.x_rows(case, 0, 512)
     assert np.array_equal(C.x_rows(case, 100, 300), full[100:300])
+
+
+# ---------------------------------------------------------------- fp8 weights (build extension)
+def test_e4m3_table_and_rounding():
+    v = O.E4M3_VALUES
+    assert v[0x7E] == 448 and v[0x01] == 2.0 ** -9 and v[0x38] == 1.0 and np.isnan(v[0x7F]) and np.isnan(v[0xFF])
+    finite = v[:127]
+    assert np.all(np.diff(finite) > 0)  # codes 0..126 ascend
+    # every finite value round-trips, with its sign
+    codes = np.concatenate([np.arange(127), np.arange(128, 255)]).astype(np.uint8)
+    assert np.array_equal(O.e4m3_codes(v[codes]), codes)
+    # ties go to the even code, out-of-range values saturate, signed zero is kept
+    cases = [(1.0625, 0x38), (1.1875, 0x3A), (2.0 ** -10, 0x00), (1.5 * 2.0 ** -9, 0x02), (500.0, 0x7E),
+             (-1e9, 0xFE), (-0.0, 0x80), (0.0, 0x00)]
+    got = O.e4m3_codes(np.array([v for v, _ in cases], dtype=np.float32))
+    assert [int(c) for c in got] == [c for _, c in cases]
+    # midpoints between neighbours round to the even neighbour; points just off them to the nearer
+    mids = (finite[1:] + finite[:-1]) / 2
+    even = np.where(np.arange(126) % 2 == 0, np.arange(126), np.arange(1, 127))
+    assert np.array_equal(O.e4m3_codes(mids.astype(np.float32)), even.astype(np.uint8))
+
+
+def test_fp8_row_quantization_and_ffn():
+    rng = np.random.Generator(np.random.PCG64(4))
+    w = O.round_to(rng.standard_normal((64, 96)).astype(np.float32) * 0.05, "bfloat16")
+    w[3] = 0.0
+    q, s = O.quantize_rows_e4m3(w)
+    assert s[3] == 1.0 and np.all(q[3] & 0x7F == 0)
+    deq = O.E4M3_VALUES[q] * s[:, None]
+    keep = np.arange(64) != 3  # the row maximum maps to code +-448, i.e. back to itself within fp32 rounding
+    assert np.allclose(np.abs(deq).max(axis=1)[keep], np.abs(w).max(axis=1)[keep], rtol=1e-6, atol=0)
+    rel = np.abs(deq - w) / np.maximum(np.abs(w), 1e-30)
+    assert np.median(rel[w != 0]) < 2 ** -4  # 3 mantissa bits
+    x = O.round_to(rng.standard_normal((5, 96)).astype(np.float32), "bfloat16")
+    w2 = O.round_to(rng.standard_normal((40, 64)).astype(np.float32) * 0.1, "bfloat16")
+    q2, s2 = O.quantize_rows_e4m3(w2)
+    got = O.from_bits(O.ffn_fp8_weights(x, q, s, q2, s2, "bfloat16"), "bfloat16")
+    ref = O.from_bits(O.ffn(x, O.E4M3_VALUES[q] * s[:, None], O.E4M3_VALUES[q2] * s2[:, None], "bfloat16",
+                            staged=True, rational=True), "bfloat16")
+    assert np.abs(got - ref).max() <= 2 ** -6 * np.abs(ref).max()
