@@ -27,7 +27,7 @@ NOALLOC_SCRATCH_BYTES = 32 << 20
 
 DTYPES = {"float16": 0, "bfloat16": 1}
 DOWN_IMPL_CODES = {"basic": 0, "full_load_a": 1, "full_load_b": 2, "streamk": 3}
-GELU_CODES = {"rational": 0, "erf": 1}
+GELU_CODES = {"rational": 0, "erf": 1, "silu": 2}  # hidden-layer activation (problem field `gelu`)
 # Kernel variants selectable through prepare_ffn(..., tile=...) (None = automatic).
 TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5,
                  "swap16k4": 6, "swap64k2": 7, "rowblock64": 8, "rowblock128": 9, "rowblock256": 10,
@@ -90,7 +90,8 @@ class Buffers(ctypes.Structure):
                 ("ldh", ctypes.c_int64), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
                 ("workspace", ctypes.c_void_p), ("counters", ctypes.c_void_p), ("flags", ctypes.c_void_p),
                 ("status", ctypes.c_void_p),
-                ("w1_scale", ctypes.c_void_p), ("w2_scale", ctypes.c_void_p)]
+                ("w1_scale", ctypes.c_void_p), ("w2_scale", ctypes.c_void_p),
+                ("bias1", ctypes.c_void_p), ("bias2", ctypes.c_void_p)]
 
 
 _lock = threading.Lock()

@@ -44,6 +44,7 @@ class PreparedFFN:
     preparation: dict
     stream: object
     weight_scales: tuple = None  # fp8 weights: (W1 row scales [H], W2 row scales [N]); storage[1:3] hold the codes
+    biases: tuple = None  # (bias1 [H] or None, bias2 [N] or None), 16-byte aligned device copies
 
     def _output_view(self):
         p = self.plan.problem
@@ -106,10 +107,12 @@ class PreparedFFN:
             sync = torch.zeros(int(k["counter_words"]) + int(k["flag_words"]) + 4, dtype=torch.int32, device=dev)
             cnt, flg, st = sync[:k["counter_words"]], sync[k["counter_words"]:-4], sync[-4:]
             sc = self.weight_scales
+            b1, b2 = self.biases or (None, None)
             bufs = _lib.Buffers(x2d[lo].data_ptr(), x2d.stride(0), w1.data_ptr(), w1.stride(0), w2.data_ptr(),
                                 w2.stride(0), hidden[lo].data_ptr(), hidden.stride(0), out[lo].data_ptr(),
                                 out.stride(0), ws.data_ptr(), cnt.data_ptr(), flg.data_ptr(), st.data_ptr(),
-                                sc[0].data_ptr() if sc else None, sc[1].data_ptr() if sc else None)
+                                sc[0].data_ptr() if sc else None, sc[1].data_ptr() if sc else None,
+                                b1.data_ptr() if b1 is not None else None, b2.data_ptr() if b2 is not None else None)
             prob = problem_struct(sub, self.plan.selection.down_impl, self.plan.gelu, plan.block_num, sms,
                                   o.get("tile"), o.get("raster_group"), o.get("l2_policy"), o.get("schedule"),
                                   o.get("weight_format"))
@@ -299,9 +302,28 @@ def _map_prepare_error(rc):
     return KernelCompilationError(f"prepare_ffn: {msg}")
 
 
+def _prepared_bias(bias, features, x, name):
+    """A bias vector as a contiguous, 16-byte aligned device tensor of x's dtype, or None."""
+    import torch
+
+    if bias is None:
+        return None
+    if not isinstance(bias, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor or None")
+    if bias.dtype != x.dtype or bias.device != x.device or tuple(bias.shape) != (features,):
+        raise ValueError(f"{name} must be a [{features}] tensor of the input's dtype on its device")
+    if bias.requires_grad:
+        raise ValueError(f"{name} must not require grad")
+    if bias.is_contiguous() and bias.data_ptr() % 16 == 0:
+        return bias
+    out = torch.empty(features + 8, dtype=bias.dtype, device=bias.device)[:features]
+    out.copy_(bias)
+    return out
+
+
 def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", block_num=None,
                 layout="linear", gelu="rational", tile=None, raster_group=None, l2_policy=None, schedule=None,
-                weight_format=None):
+                weight_format=None, activation="gelu", bias1=None, bias2=None):
     """Validates, plans and prepares storage and the launch handle without launching the FFN
     (reference ops/api.py:48-89).
 
@@ -314,17 +336,28 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
     (``quantize_weights_fp8``) and runs the tiles that widen them on chip: half the weight
     bytes, a weight-quantization error on top of the reference arithmetic.  Storage copies
     are device work timed separately as ``preparation['auxiliary_device_interval_ms']``.
+
+    Beyond the reference's V1: ``activation='silu'`` replaces the GELU by SiLU, and
+    ``bias1`` [H] / ``bias2`` [N] (input dtype) are added to the fp32 sums before the
+    activation / before the final rounding.
     """
     import torch
 
     p = validate_tensors(x, weight1, weight2, layout=layout, require_cuda=True)
+    if activation not in ("gelu", "silu"):
+        raise ValueError("activation must be 'gelu' or 'silu'")
+    if gelu not in ("rational", "erf"):
+        raise ValueError("gelu must be 'rational' or 'erf'")
+    act = "silu" if activation == "silu" else gelu
+    b1 = _prepared_bias(bias1, p.h, x, "bias1")
+    b2 = _prepared_bias(bias2, p.n, x, "bias2")
     selection = Selection(up_impl, down_impl)
     try:
         lib = _lib.load()
     except (OSError, RuntimeError) as exc:
         raise KernelCompilationError(f"{type(exc).__name__}: {exc}") from exc
     props = torch.cuda.get_device_properties(x.device)
-    plan = make_plan(p, selection, block_num, gelu=gelu, sm_count=props.multi_processor_count, tile=tile,
+    plan = make_plan(p, selection, block_num, gelu=act, sm_count=props.multi_processor_count, tile=tile,
                      raster_group=raster_group, l2_policy=l2_policy, schedule=schedule, weight_format=weight_format)
     if (props.major, props.minor) != (10, 0):
         raise RuntimeError("This implementation targets B200 (sm_100) only")
@@ -347,8 +380,9 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
         bufs = _lib.Buffers(x2d.data_ptr(), x2d.stride(0), w1.data_ptr(), w1.stride(0), w2.data_ptr(), w2.stride(0),
                             hidden.data_ptr(), hidden.stride(0), out.data_ptr(), out.stride(0), ws.data_ptr(),
                             counters.data_ptr(), flags.data_ptr(), status.data_ptr(),
-                            scales[0].data_ptr() if scales else None, scales[1].data_ptr() if scales else None)
-        prob = problem_struct(p, down_impl, gelu, plan.block_num, props.multi_processor_count, tile, raster_group,
+                            scales[0].data_ptr() if scales else None, scales[1].data_ptr() if scales else None,
+                            b1.data_ptr() if b1 is not None else None, b2.data_ptr() if b2 is not None else None)
+        prob = problem_struct(p, down_impl, act, plan.block_num, props.multi_processor_count, tile, raster_group,
                               l2_policy, schedule, weight_format)
         handle = ctypes.c_void_p()
         before = perf_counter()
@@ -359,7 +393,7 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
                        "compile_wall_ms": (perf_counter() - before) * 1000}
     provenance = kernel_provenance(down_impl)
     provenance["plan"] = plan.kernel
-    return PreparedFFN(plan, storage, handle, provenance, preparation, stream, scales)
+    return PreparedFFN(plan, storage, handle, provenance, preparation, stream, scales, (b1, b2))
 
 
 def ffn(x, weight1, weight2, **configuration):

@@ -54,12 +54,16 @@ constexpr Variant kVariants[] = {
 constexpr int kNumVariants = 12;
 constexpr int kFirstRowblock = 7;
 
-template <int BN, int ST, bool SW, bool PR, int KS, int EP, bool W8>
-KernelFn pick_kernel(int bf16, int gelu) {
+template <int BN, int ST, bool SW, bool PR, int KS, int EP, bool W8, bool B16>
+KernelFn pick_kernel_act(int act) {
   using namespace ffnb200;
-  if (bf16)
-    return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, EP, true, 1, W8> : ffn_fused_kernel<BN, ST, SW, PR, KS, EP, true, 0, W8>;
-  return gelu ? ffn_fused_kernel<BN, ST, SW, PR, KS, EP, false, 1, W8> : ffn_fused_kernel<BN, ST, SW, PR, KS, EP, false, 0, W8>;
+  if (act == 2) return ffn_fused_kernel<BN, ST, SW, PR, KS, EP, B16, 2, W8>;
+  if (act == 1) return ffn_fused_kernel<BN, ST, SW, PR, KS, EP, B16, 1, W8>;
+  return ffn_fused_kernel<BN, ST, SW, PR, KS, EP, B16, 0, W8>;
+}
+template <int BN, int ST, bool SW, bool PR, int KS, int EP, bool W8>
+KernelFn pick_kernel(int bf16, int act) {
+  return bf16 ? pick_kernel_act<BN, ST, SW, PR, KS, EP, W8, true>(act) : pick_kernel_act<BN, ST, SW, PR, KS, EP, W8, false>(act);
 }
 #define FFN_B200_VARIANTS(X)                  \
   X(0, 256, 4, false, false, 1, 4, false)     \
@@ -72,10 +76,13 @@ KernelFn pick_kernel(int bf16, int gelu) {
   X(10, 16, 6, true, false, 2, 8, true)       \
   X(11, 64, 4, true, false, 2, 8, true)
 template <int NY>
-KernelFn pick_rowblock(int bf16, int gelu) {
+KernelFn pick_rowblock(int bf16, int act) {
   using namespace ffnb200;
-  if (bf16) return gelu ? ffn_rowblock_kernel<NY, 4, true, 1> : ffn_rowblock_kernel<NY, 4, true, 0>;
-  return gelu ? ffn_rowblock_kernel<NY, 4, false, 1> : ffn_rowblock_kernel<NY, 4, false, 0>;
+  if (bf16)
+    return act == 2 ? ffn_rowblock_kernel<NY, 4, true, 2>
+                    : (act == 1 ? ffn_rowblock_kernel<NY, 4, true, 1> : ffn_rowblock_kernel<NY, 4, true, 0>);
+  return act == 2 ? ffn_rowblock_kernel<NY, 4, false, 2>
+                  : (act == 1 ? ffn_rowblock_kernel<NY, 4, false, 1> : ffn_rowblock_kernel<NY, 4, false, 0>);
 }
 KernelFn kernel_for(int variant, int bf16, int gelu) {
   switch (variant) {
@@ -311,7 +318,8 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   if (pr->k > 65535 || pr->h > 65535 || pr->n > 65535 || pr->m > (int64_t(1) << 31) - 16)
     return FFN_B200_ERR_INVALID;
   if (pr->dtype != FFN_B200_F16 && pr->dtype != FFN_B200_BF16) return FFN_B200_ERR_INVALID;
-  if (pr->gelu != FFN_B200_GELU_RATIONAL && pr->gelu != FFN_B200_GELU_ERF) return FFN_B200_ERR_INVALID;
+  if (pr->gelu != FFN_B200_GELU_RATIONAL && pr->gelu != FFN_B200_GELU_ERF && pr->gelu != FFN_B200_SILU)
+    return FFN_B200_ERR_INVALID;
   if (pr->down_impl < 0 || pr->down_impl > 3) return FFN_B200_ERR_INVALID;
   if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_B) return FFN_B200_ERR_UNAVAILABLE;
   int sm = pr->sm_count;
@@ -447,6 +455,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     if (!aligned16(p)) return FFN_B200_ERR_ALIGNMENT;
   if (!b->counters || !b->flags || !b->status) return FFN_B200_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(b->counters) & 7u) return FFN_B200_ERR_ALIGNMENT;
+  if ((b->bias1 && !aligned16(b->bias1)) || (b->bias2 && !aligned16(b->bias2))) return FFN_B200_ERR_ALIGNMENT;
   const int64_t pitches[] = {b->ldx, b->ldw1, b->ldw2, rowblock ? b->ldy : b->ldh, b->ldy};
   for (int64_t p : pitches)
     if (p <= 0 || (p % 8) != 0) return FFN_B200_ERR_ALIGNMENT;
@@ -513,6 +522,8 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     delete h;
     return rc;
   }
+  P.bias1 = static_cast<const uint16_t*>(b->bias1);
+  P.bias2 = static_cast<const uint16_t*>(b->bias2);
   P.hidden = b->hidden;
   P.y = b->y;
   P.ldh = b->ldh;

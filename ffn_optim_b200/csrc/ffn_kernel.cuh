@@ -89,6 +89,8 @@ struct Params {
                                // 0: owner c takes tiles c, c + C, ...
   const float* w1_scale;       // fp8 weights: per-row fp32 scales of W1 [H] and W2 [N]
   const float* w2_scale;
+  const uint16_t* bias1;       // optional [H] / [N] biases in the input dtype, added in fp32 to
+  const uint16_t* bias2;       // the hidden sums before the activation / to Y before rounding
   // Fused reduce-scatter of the down phase across `rs_world` GPUs (tensor parallel over H):
   // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
   // of another rank's band is pushed as a bf16 partial into that rank's staging buffer over
@@ -464,10 +466,14 @@ __device__ __forceinline__ float gelu_rational(float z) {
 __device__ __forceinline__ float gelu_erf(float z) {
   return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f));
 }
+// SiLU (the swish activation): z * sigmoid(z) with CUDA's __expf and __fdividef.
+__device__ __forceinline__ float silu(float z) { return __fdividef(z, 1.0f + __expf(-z)); }
+// Activation of the hidden layer: 0 the rational GELU, 1 the exact-erf GELU, 2 SiLU.
 template <int GELU>
 __device__ __forceinline__ float gelu(float z) {
   if constexpr (GELU == 0) return gelu_rational(z);
-  else return gelu_erf(z);
+  else if constexpr (GELU == 1) return gelu_erf(z);
+  else return silu(z);
 }
 // Packed fp32 pairs (sm_100 fma/mul/add .f32x2): each lane is one IEEE fp32 operation
 // rounded to nearest, so a pair evaluates exactly what two scalar operations would.
@@ -527,10 +533,11 @@ __device__ __forceinline__ void gelu2(float& a, float& b) {
   if constexpr (GELU == 0) {
     gelu_rational2(a, b);
   } else {
-    a = gelu_erf(a);
-    b = gelu_erf(b);
+    a = gelu<GELU>(a);
+    b = gelu<GELU>(b);
   }
 }
+
 // Two e4m3 codes (low byte: the lower-addressed element) -> two fp16 (exact) or bf16 (exact:
 // every e4m3 value is a normal fp16 and a bf16) in one 32-bit word, low half first.
 template <bool BF16>
@@ -573,6 +580,28 @@ __device__ __forceinline__ uint16_t cvt1(float a) {
   } else {
     __half h = __float2half_rn(a);
     return *reinterpret_cast<uint16_t*>(&h);
+  }
+}
+// Bias of W consecutive features starting at `c0` (16-bit values, widened to fp32), added to
+// v; features at or beyond `count` get none (ragged tiles).  Vector loads when the whole run
+// is inside (c0 is a multiple of 64 and the bias 16-byte aligned).
+template <bool BF16, int W>
+__device__ __forceinline__ void add_bias(float* v, const uint16_t* bias, int c0, int count) {
+  if (c0 + W <= count) {
+#pragma unroll
+    for (int q = 0; q < W / 8; ++q) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(bias + c0) + q);
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[8 * q + 2 * e] += unpack_lo<BF16>(wv[e]);
+        v[8 * q + 2 * e + 1] += unpack_hi<BF16>(wv[e]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < W; ++j)
+      if (c0 + j < count) v[j] += unpack_lo<BF16>(static_cast<uint32_t>(__ldg(bias + c0 + j)));
   }
 }
 
@@ -1436,9 +1465,11 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             }
           }
           if (u.phase == 0) {
+            if (p.bias1) add_bias<BF16, 64>(v, p.bias1, tq * BN + ch * 64, p.H);
 #pragma unroll
             for (int j = 0; j < 64; j += 2) gelu2<GELU>(v[j], v[j + 1]);
           }
+          if (u.phase == 1 && p.bias2 && !rs_push && !rs_reduce) add_bias<BF16, 64>(v, p.bias2, tq * BN + ch * 64, p.N);
           if (rs_reduce) {
             // Ascending rank order: sum = p_0 + p_1 + ... (this rank's fp32 partial in place),
             // 16 columns at a time to keep the register peak of the chunk loop.
@@ -1468,6 +1499,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) v[16 * q + j] = acc[j];
             }
+            // (the band owner adds the bias once, to the sum of all ranks' partials)
+            if (p.bias2) add_bias<BF16, 64>(v, p.bias2, tq * BN + ch * 64, p.N);
           }
           uint32_t pk[32];
 #pragma unroll
@@ -1541,6 +1574,14 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
               const float sc = __ldg((u.phase ? p.w2_scale : p.w1_scale) + feat);
 #pragma unroll
               for (int j = 0; j < kCW; ++j) v[j] *= sc;
+            }
+          }
+          {
+            const uint16_t* bias = u.phase ? p.bias2 : p.bias1;
+            if (bias && feat < F) {  // rows are features here: one bias value per row
+              const float b = unpack_lo<BF16>(static_cast<uint32_t>(__ldg(bias + feat)));
+#pragma unroll
+              for (int j = 0; j < kCW; ++j) v[j] += b;
             }
           }
           if (feat < F) {

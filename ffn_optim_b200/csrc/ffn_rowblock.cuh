@@ -286,6 +286,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         __syncwarp();
         if (lane == 0) mbar_arrive(uempty(a));
         ++ucnt;
+        if (p.bias1) add_bias<BF16, 32>(v, p.bias1, j * LY::kChunk + part * 32, p.H);
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -317,6 +318,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         for (int h = 0; h < 2; ++h) {
           float v[32];
           tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), v);
+          if (p.bias2) add_bias<BF16, 32>(v, p.bias2, yc * 64 + h * 32, p.N);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);

@@ -64,7 +64,9 @@ typedef enum {
 /* GELU form used in the up-projection epilogue.  RATIONAL is the reference kernel's
  * clipped rational erf (ops/kernel/ffn.py:548-572, validation/reference.py:5-13);
  * ERF calls CUDA's erff. */
-typedef enum { FFN_B200_GELU_RATIONAL = 0, FFN_B200_GELU_ERF = 1 } ffn_b200_gelu;
+/* Activation of the hidden layer (the problem's `gelu` field): the reference kernel's rational
+ * GELU, the exact-erf GELU, or SiLU (z * sigmoid(z); beyond the reference's V1). */
+typedef enum { FFN_B200_GELU_RATIONAL = 0, FFN_B200_GELU_ERF = 1, FFN_B200_SILU = 2 } ffn_b200_gelu;
 
 /* Weight storage: the input dtype, or fp8 e4m3 codes with one fp32 scale per row
  * (W[r, c] = code[r, c] * scale[r]; see ffn_b200_quantize_fp8_rows).  fp8 weights are
@@ -152,6 +154,10 @@ typedef struct {
   int32_t* status;
   const float* w1_scale; /* FFN_B200_WEIGHTS_FP8_ROWS: [H] and [N] fp32 row scales, else NULL */
   const float* w2_scale;
+  const void* bias1;     /* optional [H] and [N] biases in the input dtype (16-byte aligned), or
+                            NULL: hidden = act(X.W1^T + b1), Y = hidden.W2^T + b2, each bias
+                            added to the fp32 sum (beyond the reference's V1) */
+  const void* bias2;
 } ffn_b200_buffers;
 
 typedef struct ffn_b200_handle ffn_b200_handle;

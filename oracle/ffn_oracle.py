@@ -104,19 +104,36 @@ def round_to(a, dtype):
     return from_bits(to_bits(a, dtype), dtype)
 
 
-def ffn(x, w1, w2, dtype, *, staged=False, rational=False):
+def silu(z):
+    """SiLU in float32: z * sigmoid(z) = z / (1 + exp(-z)) (build extension beyond the
+    reference's V1)."""
+    z = np.asarray(z, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        return (z / (np.float32(1) + np.exp(-z))).astype(np.float32)
+
+
+def ffn(x, w1, w2, dtype, *, staged=False, rational=False, b1=None, b2=None, activation="gelu"):
     """Oracle of validation/reference.py:16-23 on float32 arrays holding ``dtype`` values.
 
     ``x`` is [..., K] (already restricted to the rows of interest), ``w1`` [H, K],
-    ``w2`` [N, H].  Returns the output's uint16 bit patterns, shape [..., N].
+    ``w2`` [N, H].  Returns the output's uint16 bit patterns, shape [..., N].  Build
+    extensions (not in the reference): optional biases ``b1`` [H] / ``b2`` [N] added to the
+    fp32 sums (before the activation / before the final rounding), ``activation='silu'``.
     """
     x = np.asarray(x, dtype=np.float32)
     lead = x.shape[:-1]
     z = x.reshape(-1, x.shape[-1]) @ np.asarray(w1, dtype=np.float32).T
-    hidden = gelu_rational(z) if rational else gelu_erf(z)
+    if b1 is not None:
+        z = (z + np.asarray(b1, dtype=np.float32)).astype(np.float32)
+    if activation == "silu":
+        hidden = silu(z)
+    else:
+        hidden = gelu_rational(z) if rational else gelu_erf(z)
     if staged:
         hidden = round_to(hidden, dtype)
     y = hidden @ np.asarray(w2, dtype=np.float32).T
+    if b2 is not None:
+        y = (y + np.asarray(b2, dtype=np.float32)).astype(np.float32)
     return to_bits(y, dtype).reshape(*lead, w2.shape[0])
 
 
