@@ -27,7 +27,7 @@ NOALLOC_SCRATCH_BYTES = 32 << 20
 
 DTYPES = {"float16": 0, "bfloat16": 1}
 DOWN_IMPL_CODES = {"basic": 0, "full_load_a": 1, "full_load_b": 2, "streamk": 3}
-GELU_CODES = {"rational": 0, "erf": 1, "silu": 2}  # hidden-layer activation (problem field `gelu`)
+GELU_CODES = {"rational": 0, "erf": 1, "silu": 2, "swiglu": 3}  # hidden-layer activation (problem field `gelu`)
 # Kernel variants selectable through prepare_ffn(..., tile=...) (None = automatic).
 TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5,
                  "swap16k4": 6, "swap64k2": 7, "rowblock64": 8, "rowblock128": 9, "rowblock256": 10,
@@ -44,7 +44,7 @@ KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-b
 EXPORTED = ("ffn_b200_abi_version", "ffn_b200_strerror", "ffn_b200_device_info", "ffn_b200_make_plan",
             "ffn_b200_prepare", "ffn_b200_run", "ffn_b200_rebind_io", "ffn_b200_reset",
             "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_set_trace",
-            "ffn_b200_set_owner_map", "ffn_b200_get_owner_map", "ffn_b200_quantize_fp8_rows", "ffn_b200_get_plan",
+            "ffn_b200_set_owner_map", "ffn_b200_get_owner_map", "ffn_b200_quantize_fp8_rows", "ffn_b200_get_plan", "ffn_b200_swiglu_rows",
             "ffn_b200_destroy", "ffn_b200_launch", "ffn_b200_run_noalloc", "ffn_b200_peer_alloc",
             "ffn_b200_peer_open", "ffn_b200_peer_close", "ffn_b200_peer_free", "ffn_b200_reduce_scatter_bytes",
             "ffn_b200_set_reduce_scatter")
@@ -135,6 +135,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             "ffn_b200_get_owner_map": ([vp, vp, i32, vp], i32),
             "ffn_b200_quantize_fp8_rows": ([vp, i64, i32, i64, i64, vp, i64, vp, vp], i32),
             "ffn_b200_get_plan": ([vp, ctypes.POINTER(PlanInfo)], i32),
+            "ffn_b200_swiglu_rows": ([i64, i32], i64),
             "ffn_b200_destroy": ([vp], i32),
             "ffn_b200_launch": ([ctypes.POINTER(Problem), ctypes.POINTER(Buffers), vp], i32),
             "ffn_b200_run_noalloc": ([ctypes.POINTER(Problem), vp, i64, vp, i64, vp, i64, vp, i64, vp, vp], i32),

@@ -12,8 +12,8 @@ from dataclasses import dataclass
 from time import perf_counter
 
 from . import _lib
-from .host.dispatch import Selection, kernel_provenance
-from .host.inputs import prepare_storage, quantize_weights_fp8, validate_tensors
+from .host.dispatch import NotApplicable, Selection, kernel_provenance
+from .host.inputs import pack_swiglu, prepare_storage, quantize_weights_fp8, validate_tensors
 from .host.tiling import make_plan, problem_struct
 
 
@@ -102,6 +102,8 @@ class PreparedFFN:
                              tile=o.get("tile"), raster_group=o.get("raster_group"), l2_policy=o.get("l2_policy"),
                              schedule=o.get("schedule"), weight_format=o.get("weight_format"))
             k = plan.kernel
+            if self.plan.gelu == "swiglu" and k["swap_ab"] != self.plan.kernel["swap_ab"]:
+                raise NotApplicable("run_host: a chunk's tiles need another SwiGLU row order of W1")
             if k["workspace_floats"] > ws.numel():
                 ws = torch.empty(int(k["workspace_floats"]), dtype=torch.float32, device=dev)
             sync = torch.zeros(int(k["counter_words"]) + int(k["flag_words"]) + 4, dtype=torch.int32, device=dev)
@@ -337,18 +339,30 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
     bytes, a weight-quantization error on top of the reference arithmetic.  Storage copies
     are device work timed separately as ``preparation['auxiliary_device_interval_ms']``.
 
-    Beyond the reference's V1: ``activation='silu'`` replaces the GELU by SiLU, and
-    ``bias1`` [H] / ``bias2`` [N] (input dtype) are added to the fp32 sums before the
-    activation / before the final rounding.
+    Beyond the reference's V1: ``activation='silu'`` replaces the GELU by SiLU;
+    ``activation='swiglu'`` takes ``weight1 = [W_gate; W_up]`` ([2H, K]) and computes
+    ``hidden = SiLU(x W_gate^T) * (x W_up^T)``; ``bias1`` [H] / ``bias2`` [N] (input dtype) are
+    added to the fp32 sums before the activation / before the final rounding (``bias1`` not
+    with SwiGLU).
     """
     import torch
 
-    p = validate_tensors(x, weight1, weight2, layout=layout, require_cuda=True)
-    if activation not in ("gelu", "silu"):
-        raise ValueError("activation must be 'gelu' or 'silu'")
+    if activation not in ("gelu", "silu", "swiglu"):
+        raise ValueError("activation must be 'gelu', 'silu' or 'swiglu'")
     if gelu not in ("rational", "erf"):
         raise ValueError("gelu must be 'rational' or 'erf'")
-    act = "silu" if activation == "silu" else gelu
+    glu = activation == "swiglu"
+    if glu:
+        # W1 = [gate rows; up rows], [2H, K]; validated as the gate half against W2 [N, H]
+        if not isinstance(weight1, torch.Tensor) or weight1.dim() != 2 or isinstance(weight2, torch.Tensor) and (
+                weight2.dim() != 2 or weight1.shape[0] != 2 * weight2.shape[1]):
+            raise ValueError("activation='swiglu' takes weight1 = [gate; up] of shape [2H, K] and weight2 [N, H]")
+        if bias1 is not None:
+            raise ValueError("bias1 is not supported with activation='swiglu'")
+        p = validate_tensors(x, weight1[:weight2.shape[1]], weight2, layout=layout, require_cuda=True)
+    else:
+        p = validate_tensors(x, weight1, weight2, layout=layout, require_cuda=True)
+    act = activation if activation != "gelu" else gelu
     b1 = _prepared_bias(bias1, p.h, x, "bias1")
     b2 = _prepared_bias(bias2, p.n, x, "bias2")
     selection = Selection(up_impl, down_impl)
@@ -368,6 +382,8 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         scales = None
+        if glu:  # the kernel's gate/up row order
+            weight1 = pack_swiglu(weight1, p.h, plan.kernel["swap_ab"])
         if weight_format == "fp8":
             q1, s1 = quantize_weights_fp8(weight1)
             q2, s2 = quantize_weights_fp8(weight2)

@@ -57,6 +57,7 @@ constexpr int kFirstRowblock = 7;
 template <int BN, int ST, bool SW, bool PR, int KS, int EP, bool W8, bool B16>
 KernelFn pick_kernel_act(int act) {
   using namespace ffnb200;
+  if (act == 3) return ffn_fused_kernel<BN, ST, SW, PR, KS, EP, B16, 3, W8>;
   if (act == 2) return ffn_fused_kernel<BN, ST, SW, PR, KS, EP, B16, 2, W8>;
   if (act == 1) return ffn_fused_kernel<BN, ST, SW, PR, KS, EP, B16, 1, W8>;
   return ffn_fused_kernel<BN, ST, SW, PR, KS, EP, B16, 0, W8>;
@@ -311,6 +312,11 @@ int ffn_b200_device_info(int device, int* sm_count, int* cc_major, int* cc_minor
   return FFN_B200_OK;
 }
 
+int64_t ffn_b200_swiglu_rows(int64_t h, int32_t swap_ab) {
+  if (h <= 0) return 0;
+  return swap_ab ? 2 * h : 128 * ((h + 63) / 64);
+}
+
 int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   if (!pr || !out) return FFN_B200_ERR_INVALID;
   // Shape contract of ops/host/inputs.py:38-53.
@@ -318,8 +324,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   if (pr->k > 65535 || pr->h > 65535 || pr->n > 65535 || pr->m > (int64_t(1) << 31) - 16)
     return FFN_B200_ERR_INVALID;
   if (pr->dtype != FFN_B200_F16 && pr->dtype != FFN_B200_BF16) return FFN_B200_ERR_INVALID;
-  if (pr->gelu != FFN_B200_GELU_RATIONAL && pr->gelu != FFN_B200_GELU_ERF && pr->gelu != FFN_B200_SILU)
-    return FFN_B200_ERR_INVALID;
+  if (pr->gelu < FFN_B200_GELU_RATIONAL || pr->gelu > FFN_B200_SWIGLU) return FFN_B200_ERR_INVALID;
   if (pr->down_impl < 0 || pr->down_impl > 3) return FFN_B200_ERR_INVALID;
   if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_B) return FFN_B200_ERR_UNAVAILABLE;
   int sm = pr->sm_count;
@@ -338,7 +343,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
 
   std::memset(out, 0, sizeof(*out));
   if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_A) {
-    if (fp8w) return FFN_B200_ERR_NOT_APPLICABLE;
+    if (fp8w || pr->gelu == FFN_B200_SWIGLU) return FFN_B200_ERR_NOT_APPLICABLE;
     return plan_rowblock(*pr, grid, out);
   }
   if (pr->tile_variant > 0 && kVariants[pr->tile_variant - 1].rowblock) return FFN_B200_ERR_INVALID;
@@ -366,7 +371,9 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   const int ncta = v.pair ? 2 : 1;
   const int tile_m = ffnb200::kBM * ncta;
   const int C = grid / ncta;  // work-list owners (CTAs, or CTA pairs)
-  const PhaseInput up = v.swap ? PhaseInput{pr->h, pr->m, pr->k} : PhaseInput{pr->m, pr->h, pr->k};
+  // SwiGLU: the up GEMM runs over the packed gate/up rows of W1 (ffn_b200_swiglu_rows).
+  const int64_t up_rows = pr->gelu == FFN_B200_SWIGLU ? ffn_b200_swiglu_rows(pr->h, v.swap ? 1 : 0) : pr->h;
+  const PhaseInput up = v.swap ? PhaseInput{up_rows, pr->m, pr->k} : PhaseInput{pr->m, up_rows, pr->k};
   const PhaseInput dn = v.swap ? PhaseInput{pr->n, pr->m, pr->h} : PhaseInput{pr->m, pr->n, pr->h};
   // Raster group: a wave of C concurrent tiles spans `group` tile rows x C/group tile columns;
   // balancing their operand bytes (group*tile_m = (C/group)*tile_n) minimises the K-slices a
@@ -456,6 +463,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   if (!b->counters || !b->flags || !b->status) return FFN_B200_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(b->counters) & 7u) return FFN_B200_ERR_ALIGNMENT;
   if ((b->bias1 && !aligned16(b->bias1)) || (b->bias2 && !aligned16(b->bias2))) return FFN_B200_ERR_ALIGNMENT;
+  if (b->bias1 && pr->gelu == FFN_B200_SWIGLU) return FFN_B200_ERR_INVALID;  // no gate/up bias
   const int64_t pitches[] = {b->ldx, b->ldw1, b->ldw2, rowblock ? b->ldy : b->ldh, b->ldy};
   for (int64_t p : pitches)
     if (p <= 0 || (p % 8) != 0) return FFN_B200_ERR_ALIGNMENT;
@@ -483,6 +491,8 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
 
   Params& P = h->params;
   std::memset(&P, 0, sizeof(P));
+  // Rows of W1 as stored: the gate/up-packed rows for SwiGLU.
+  const int64_t w1_rows = prob.gelu == FFN_B200_SWIGLU ? ffn_b200_swiglu_rows(prob.h, plan.swap_ab) : prob.h;
   // B boxes: each CTA of a pair loads half of the tile's B rows.
   const uint32_t bn = static_cast<uint32_t>(plan.tile_n / (plan.cta_pair ? 2 : 1));
   const int dt = prob.dtype;
@@ -497,7 +507,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     if (!rc) rc = encode_2d(&P.tm_st_y, b->y, dt, prob.n, prob.m, b->ldy, 64, ffnb200::kStoreRows);
   } else if (!sw) {
     rc = encode_2d(&P.tm_a_up, b->x, dt, prob.k, prob.m, b->ldx, 64, 128);
-    if (!rc) rc = encode_2d(&P.tm_b_up, b->w1, dt, prob.k, prob.h, b->ldw1, 64, bn);
+    if (!rc) rc = encode_2d(&P.tm_b_up, b->w1, dt, prob.k, w1_rows, b->ldw1, 64, bn);
     if (!rc) rc = encode_2d(&P.tm_a_dn, b->hidden, dt, prob.h, prob.m, b->ldh, 64, 128);
     if (!rc) rc = encode_2d(&P.tm_b_dn, b->w2, dt, prob.h, prob.n, b->ldw2, 64, bn);
     if (!rc) rc = encode_2d(&P.tm_st_hid, b->hidden, dt, prob.h, prob.m, b->ldh, 64, ffnb200::kStoreRows);
@@ -506,14 +516,14 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     // fp8 weight k-blocks: 128 rows x 64 one-byte codes, 64-byte swizzle (the converter
     // warps read them bank-conflict free); the token operands as in the 16-bit decode tiles.
     const uint32_t wbox = static_cast<uint32_t>(64 * kVariants[plan.variant].ksub);  // bytes of a weight row per load
-    rc = encode_2d_u8(&P.tm_a_up, b->w1, prob.k, prob.h, b->ldw1, wbox, 128);
+    rc = encode_2d_u8(&P.tm_a_up, b->w1, prob.k, w1_rows, b->ldw1, wbox, 128);
     if (!rc) rc = encode_2d(&P.tm_b_up, b->x, dt, prob.k, prob.m, b->ldx, 64, bn);
     if (!rc) rc = encode_2d_u8(&P.tm_a_dn, b->w2, prob.h, prob.n, b->ldw2, wbox, 128);
     if (!rc) rc = encode_2d(&P.tm_b_dn, b->hidden, dt, prob.h, prob.m, b->ldh, 64, bn);
     P.w1_scale = b->w1_scale;
     P.w2_scale = b->w2_scale;
   } else {
-    rc = encode_2d(&P.tm_a_up, b->w1, dt, prob.k, prob.h, b->ldw1, 64, 128);
+    rc = encode_2d(&P.tm_a_up, b->w1, dt, prob.k, w1_rows, b->ldw1, 64, 128);
     if (!rc) rc = encode_2d(&P.tm_b_up, b->x, dt, prob.k, prob.m, b->ldx, 64, bn);
     if (!rc) rc = encode_2d(&P.tm_a_dn, b->w2, dt, prob.h, prob.n, b->ldw2, 64, 128);
     if (!rc) rc = encode_2d(&P.tm_b_dn, b->hidden, dt, prob.h, prob.m, b->ldh, 64, bn);

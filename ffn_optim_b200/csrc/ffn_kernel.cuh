@@ -468,7 +468,8 @@ __device__ __forceinline__ float gelu_erf(float z) {
 }
 // SiLU (the swish activation): z * sigmoid(z) with CUDA's __expf and __fdividef.
 __device__ __forceinline__ float silu(float z) { return __fdividef(z, 1.0f + __expf(-z)); }
-// Activation of the hidden layer: 0 the rational GELU, 1 the exact-erf GELU, 2 SiLU.
+// Activation of the hidden layer: 0 the rational GELU, 1 the exact-erf GELU, 2 SiLU;
+// 3 is SwiGLU (SiLU(gate) * up over a gate/up-packed W1), handled in the epilogues.
 template <int GELU>
 __device__ __forceinline__ float gelu(float z) {
   if constexpr (GELU == 0) return gelu_rational(z);
@@ -1444,6 +1445,9 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
                          static_cast<int>(rank) * kBM + sub * 32;
 #pragma unroll 1
         for (int ch = ch0; ch < ch0 + kMyChunks; ++ch) {
+          if constexpr (GELU == 3) {  // SwiGLU up values: consumed with their gate chunk
+            if (u.phase == 0 && (ch & 1) && u.role != kRoleContrib) continue;
+          }
           float v[64];
           tmem_ld32(tbase + ch * 64, v);
           tmem_ld32(tbase + ch * 64 + 32, v + 32);
@@ -1464,7 +1468,32 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
               }
             }
           }
-          if (u.phase == 0) {
+          int hcol = tq * BN + ch * 64;  // hidden column of this chunk (up phase)
+          if constexpr (GELU == 3) {
+            // SwiGLU: W1 rows come in blocks of 64 gate rows then the matching 64 up rows, so
+            // chunk ch (even) holds gates and chunk ch + 1 the up values of 64 hidden columns.
+            if (u.phase == 0) {
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {  // up values 32 at a time (register pressure)
+                float w[32];
+                tmem_ld32(tbase + (ch + 1) * 64 + hh * 32, w);
+                if (u.role == kRoleOwner) {
+#pragma unroll 1
+                  for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
+                    const float4* src = reinterpret_cast<const float4*>(ws_row(c2) + (ch + 1) * 64 + hh * 32);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                      const float4 t = __ldcg(src + j);
+                      w[4 * j] += t.x; w[4 * j + 1] += t.y; w[4 * j + 2] += t.z; w[4 * j + 3] += t.w;
+                    }
+                  }
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[hh * 32 + j] = silu(v[hh * 32 + j]) * w[j];
+              }
+              hcol = tq * (BN / 2) + (ch / 2) * 64;
+            }
+          } else if (u.phase == 0) {
             if (p.bias1) add_bias<BF16, 64>(v, p.bias1, tq * BN + ch * 64, p.H);
 #pragma unroll
             for (int j = 0; j < 64; j += 2) gelu2<GELU>(v[j], v[j + 1]);
@@ -1527,7 +1556,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
                                                  rs_tile) * kBM) + sub * 32;
               tma_store_2d(&p.tm_rs[rs_owner], sb, ch * 64, srow);
             } else {
-              tma_store_2d(tms, sb, tq * BN + ch * 64, orow);
+              tma_store_2d(tms, sb, u.phase ? tq * BN + ch * 64 : hcol, orow);
             }
             bulk_commit();
           }
@@ -1536,7 +1565,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
       } else {
         // Swap mode: tile rows are features (H for up, N for down), columns are tokens.
         const int feat = tr * kBM + row;
-        const int F = u.phase ? p.N : p.H;
+        const int F = u.phase ? p.N : (GELU == 3 ? 2 * p.H : p.H);  // feature rows (SwiGLU: gate/up pairs)
         uint16_t* out = reinterpret_cast<uint16_t*>(u.phase ? p.y : p.hidden);
         const long long ld = u.phase ? p.ldy : p.ldh;
 #pragma unroll 1
@@ -1582,6 +1611,26 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
               const float b = unpack_lo<BF16>(static_cast<uint32_t>(__ldg(bias + feat)));
 #pragma unroll
               for (int j = 0; j < kCW; ++j) v[j] += b;
+            }
+          }
+          if constexpr (GELU == 3) {
+            // SwiGLU in the decode tiles: W1 rows alternate gate, up (rows 2i, 2i + 1 give
+            // hidden feature i), so the up value sits in the neighbouring lane.
+            if (u.phase == 0) {
+#pragma unroll
+              for (int j = 0; j < kCW; ++j) {
+                const float up = __shfl_xor_sync(0xffffffffu, v[j], 1);
+                v[j] = silu(v[j]) * up;
+              }
+              const int hfeat = feat >> 1;
+              if ((row & 1) == 0 && hfeat < p.H) {
+#pragma unroll
+                for (int j = 0; j < kCW; ++j) {
+                  const int m = tq * BN + ch * kCW + j;
+                  if (m < p.M) out[static_cast<long long>(m) * ld + hfeat] = cvt1<BF16>(v[j]);
+                }
+              }
+              continue;
             }
           }
           if (feat < F) {

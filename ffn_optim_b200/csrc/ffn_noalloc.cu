@@ -93,6 +93,8 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   if (prob.block_num > sm) return FFN_B200_ERR_DEVICE;
   if (prob.tile_variant == 5) return FFN_B200_ERR_INVALID;  // CTA-pair tiles need a cluster launch
   if (prob.weight_format != FFN_B200_WEIGHTS_NATIVE) return FFN_B200_ERR_INVALID;  // no scale arguments here
+  // SwiGLU's W1 row order depends on the chosen tiles, which this entry point may change.
+  if (prob.gelu == FFN_B200_SWIGLU) return FFN_B200_ERR_INVALID;
   ffn_b200_plan plan;
   rc = ffn_b200_make_plan(&prob, &plan);
   if (rc) return rc;

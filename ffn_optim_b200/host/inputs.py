@@ -98,6 +98,33 @@ def _packed(t, rows, cols):
     return buf
 
 
+def pack_swiglu(weight1, hidden, swap_ab):
+    """W1 = [gate rows; up rows] ([2H, K]) in the fused kernel's SwiGLU order: with
+    ``swap_ab`` (decode tiles) gate row i at row 2i and up row i at 2i + 1; otherwise blocks
+    of 64 gate rows each followed by the matching 64 up rows, zero rows padding the last block
+    (``ffn_b200_swiglu_rows`` gives the row count)."""
+    import torch
+
+    from .. import _lib
+
+    gate, up = weight1[:hidden], weight1[hidden:]
+    k = weight1.shape[1]
+    rows = int(_lib.load().ffn_b200_swiglu_rows(hidden, 1 if swap_ab else 0))
+    packed = torch.zeros((rows, pitch_of(k)), dtype=weight1.dtype, device=weight1.device)
+    if swap_ab:
+        packed[0::2, :k] = gate
+        packed[1::2, :k] = up
+    else:
+        blocks = rows // 128
+        view = packed.view(blocks, 2, 64, packed.shape[1])
+        g = torch.zeros((blocks * 64, k), dtype=weight1.dtype, device=weight1.device)
+        u = torch.zeros_like(g)
+        g[:hidden], u[:hidden] = gate, up
+        view[:, 0, :, :k] = g.view(blocks, 64, k)
+        view[:, 1, :, :k] = u.view(blocks, 64, k)
+    return packed[:, :k]
+
+
 def quantize_weights_fp8(weight):
     """fp8 weights for the decode tiles: ``weight`` [rows, cols] (fp16/bf16, CUDA) becomes
     ``(codes, scales)``: uint8 e4m3 codes [rows, pitch] (pitch = cols rounded up to 16
@@ -143,7 +170,8 @@ def prepare_storage(x, weight1, weight2, plan):
     xs = x.reshape(p.m, p.k) if x.is_contiguous() else x.contiguous().view(p.m, p.k)
     x2d = _packed(xs, p.m, p.k)
     # (fp8 weights arrive here as uint8 code views with 16-byte pitches: used in place)
-    w1 = weight1 if _tma_ready(weight1, p.h, p.k) else _packed(weight1.contiguous(), p.h, p.k)
+    r1 = weight1.shape[0]  # H, or the gate/up-packed rows of a SwiGLU problem
+    w1 = weight1 if _tma_ready(weight1, r1, p.k) else _packed(weight1.contiguous(), r1, p.k)
     w2 = weight2 if _tma_ready(weight2, p.n, p.h) else _packed(weight2.contiguous(), p.n, p.h)
     # full_load_a keeps the hidden row block on chip: an 8-column stand-in keeps the
     # storage tuple's shape contract (row-indexable) without the M x H buffer.

@@ -65,8 +65,13 @@ typedef enum {
  * clipped rational erf (ops/kernel/ffn.py:548-572, validation/reference.py:5-13);
  * ERF calls CUDA's erff. */
 /* Activation of the hidden layer (the problem's `gelu` field): the reference kernel's rational
- * GELU, the exact-erf GELU, or SiLU (z * sigmoid(z); beyond the reference's V1). */
-typedef enum { FFN_B200_GELU_RATIONAL = 0, FFN_B200_GELU_ERF = 1, FFN_B200_SILU = 2 } ffn_b200_gelu;
+ * GELU, the exact-erf GELU, SiLU (z * sigmoid(z)), or SwiGLU (SiLU(x.Wg^T) * (x.Wu^T)); the
+ * last two are beyond the reference's V1.  For SwiGLU, h is the hidden width and W1 holds
+ * ffn_b200_swiglu_rows(h, plan.swap_ab) rows: with swap_ab == 0, blocks of 64 gate rows each
+ * followed by the matching 64 up rows (zero rows pad the last block); with swap_ab == 1, gate
+ * row i at row 2i and up row i at row 2i + 1.  W1 is then not a Linear weight of shape [h, K]:
+ * plan first, pack, then prepare (ffn_optim_b200.prepare_ffn does this). */
+typedef enum { FFN_B200_GELU_RATIONAL = 0, FFN_B200_GELU_ERF = 1, FFN_B200_SILU = 2, FFN_B200_SWIGLU = 3 } ffn_b200_gelu;
 
 /* Weight storage: the input dtype, or fp8 e4m3 codes with one fp32 scale per row
  * (W[r, c] = code[r, c] * scale[r]; see ffn_b200_quantize_fp8_rows).  fp8 weights are
@@ -252,6 +257,8 @@ FFN_B200_EXPORT int ffn_b200_get_owner_map(const ffn_b200_handle* handle, int32_
                                            int32_t* count);
 
 FFN_B200_EXPORT int ffn_b200_get_plan(const ffn_b200_handle* handle, ffn_b200_plan* plan);
+/* Rows of the packed W1 of a SwiGLU problem with hidden width h (see ffn_b200_gelu). */
+FFN_B200_EXPORT int64_t ffn_b200_swiglu_rows(int64_t h, int32_t swap_ab);
 FFN_B200_EXPORT int ffn_b200_destroy(ffn_b200_handle* handle);
 
 /* Device scratch held by the library itself for ffn_b200_run_noalloc (hidden activations,

@@ -118,7 +118,9 @@ def ffn(x, w1, w2, dtype, *, staged=False, rational=False, b1=None, b2=None, act
     ``x`` is [..., K] (already restricted to the rows of interest), ``w1`` [H, K],
     ``w2`` [N, H].  Returns the output's uint16 bit patterns, shape [..., N].  Build
     extensions (not in the reference): optional biases ``b1`` [H] / ``b2`` [N] added to the
-    fp32 sums (before the activation / before the final rounding), ``activation='silu'``.
+    fp32 sums (before the activation / before the final rounding), ``activation='silu'``,
+    and ``activation='swiglu'`` with ``w1`` = [gate rows; up rows] ([2H, K]):
+    hidden = SiLU(x gate^T) * (x up^T).
     """
     x = np.asarray(x, dtype=np.float32)
     lead = x.shape[:-1]
@@ -127,6 +129,9 @@ def ffn(x, w1, w2, dtype, *, staged=False, rational=False, b1=None, b2=None, act
         z = (z + np.asarray(b1, dtype=np.float32)).astype(np.float32)
     if activation == "silu":
         hidden = silu(z)
+    elif activation == "swiglu":  # w1 = [gate rows; up rows], [2H, K]
+        h = z.shape[1] // 2
+        hidden = (silu(z[:, :h]) * z[:, h:]).astype(np.float32)
     else:
         hidden = gelu_rational(z) if rational else gelu_erf(z)
     if staged:

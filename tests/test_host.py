@@ -276,3 +276,34 @@ def test_c_planner_rejects_bad_problems(lib):
     h = ctypes.c_void_p()
     prob = _lib.Problem(64, 64, 64, 64, 1, 0, 0, 0, 148)
     assert lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), 0, ctypes.byref(h)) != 0
+
+
+def test_swiglu_packing_and_plan(lib):
+    """SwiGLU's packed W1: ffn_b200_swiglu_rows, the two row orders of pack_swiglu (checked on
+    CPU tensors against an index restatement), and the up GEMM planned over the packed rows."""
+    from ffn_optim_b200.host.inputs import pack_swiglu
+
+    assert lib.ffn_b200_swiglu_rows(520, 0) == 128 * 9 and lib.ffn_b200_swiglu_rows(520, 1) == 1040
+    assert lib.ffn_b200_swiglu_rows(0, 0) == 0
+    h, k = 130, 24
+    w1 = torch.arange(2 * h * k, dtype=torch.float32).reshape(2 * h, k).to(torch.bfloat16)
+    for swap in (0, 1):
+        packed = pack_swiglu(w1, h, swap)
+        assert packed.shape == (lib.ffn_b200_swiglu_rows(h, swap), k)
+        for r in range(packed.shape[0]):
+            if swap:
+                src = (r % 2) * h + r // 2
+            else:
+                i = (r // 128) * 64 + r % 64  # hidden column of the row
+                src = (h + i if (r // 64) % 2 else i) if i < h else None
+            want = w1[src] if src is not None else torch.zeros(k, dtype=w1.dtype)
+            assert torch.equal(packed[r], want), (swap, r)
+    info = _lib.PlanInfo()
+    for tile, rows, swap in ((1, 128 * 9, 0), (3, 1040, 1)):  # cta128x256, swap16
+        prob = _lib.Problem(16, 64, 520, 64, 1, 0, _lib.GELU_CODES["swiglu"], 0, 148, tile)
+        assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.OK
+        assert info.swap_ab == swap
+        up = info.up.tiles_r if swap else info.up.tiles_q
+        assert up == -(-rows // (128 if swap else info.tile_n))
+    prob = _lib.Problem(16, 64, 520, 64, 1, 1, _lib.GELU_CODES["swiglu"], 0, 148)  # full_load_a
+    assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_NOT_APPLICABLE
