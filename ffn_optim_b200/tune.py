@@ -68,6 +68,11 @@ def time_prepared(prepared, warmup=5, repeats=20):
     prepared.check()
     pairs = []
     with torch.cuda.device(prepared.storage[0].device):
+        # A device-side delay ahead of the timed launches keeps the stream's queue filled, so
+        # each start event fires when the previous run ends rather than when the host gets
+        # to the next launch (for short kernels the host launch would otherwise be timed).
+        with torch.cuda.stream(prepared.stream):
+            torch.cuda._sleep(100_000 * repeats)
         for _ in range(repeats):
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record(prepared.stream)
