@@ -44,6 +44,7 @@ KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-b
 EXPORTED = ("ffn_b200_abi_version", "ffn_b200_strerror", "ffn_b200_device_info", "ffn_b200_make_plan",
             "ffn_b200_prepare", "ffn_b200_run", "ffn_b200_rebind_io", "ffn_b200_reset",
             "ffn_b200_set_wait_limit", "ffn_b200_set_fault_injection", "ffn_b200_set_trace",
+            "ffn_b200_set_launch_overlap",
             "ffn_b200_set_owner_map", "ffn_b200_get_owner_map", "ffn_b200_quantize_fp8_rows", "ffn_b200_get_plan", "ffn_b200_swiglu_rows",
             "ffn_b200_destroy", "ffn_b200_launch", "ffn_b200_run_noalloc", "ffn_b200_peer_alloc",
             "ffn_b200_peer_open", "ffn_b200_peer_close", "ffn_b200_peer_free", "ffn_b200_reduce_scatter_bytes",
@@ -131,6 +132,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             "ffn_b200_set_wait_limit": ([vp, u64], i32),
             "ffn_b200_set_fault_injection": ([vp, i32], i32),
             "ffn_b200_set_trace": ([vp, vp], i32),
+            "ffn_b200_set_launch_overlap": ([vp, i32], i32),
             "ffn_b200_set_owner_map": ([vp, vp], i32),
             "ffn_b200_get_owner_map": ([vp, vp, i32, vp], i32),
             "ffn_b200_quantize_fp8_rows": ([vp, i64, i32, i64, i64, vp, i64, vp, vp], i32),

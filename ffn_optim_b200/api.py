@@ -45,6 +45,7 @@ class PreparedFFN:
     stream: object
     weight_scales: tuple = None  # fp8 weights: (W1 row scales [H], W2 row scales [N]); storage[1:3] hold the codes
     biases: tuple = None  # (bias1 [H] or None, bias2 [N] or None), 16-byte aligned device copies
+    launch_overlap: bool = False  # see set_launch_overlap
 
     def _output_view(self):
         p = self.plan.problem
@@ -122,6 +123,8 @@ class PreparedFFN:
             rc = lib.ffn_b200_prepare(ctypes.byref(prob), ctypes.byref(bufs), dev.index or 0, ctypes.byref(h))
             if rc != _lib.OK:
                 raise _map_prepare_error(rc)
+            if self.launch_overlap:
+                lib.ffn_b200_set_launch_overlap(h, 1)
             handles.append((lo, hi, h, (ws, sync)))
             lo = hi
         self._chunks = (chunks, handles)
@@ -213,6 +216,18 @@ class PreparedFFN:
         rc = _lib.load().ffn_b200_set_wait_limit(self.handle, int(seconds * 1e9))
         if rc != _lib.OK:
             raise ValueError(f"set_wait_limit: {_lib.strerror(rc)}")
+
+    def set_launch_overlap(self, enable: bool = True):
+        """Overlapped launches (programmatic dependent launch): each later ``run()`` sets up
+        while the stream's previous kernel finishes and touches global memory only after
+        that kernel completed, so results and ordering are those of serial launches; saves
+        the launch gap of back-to-back calls.  Off by default."""
+        handles = [self.handle] + [h for _, _, h, _ in (getattr(self, "_chunks", None) or (0, []))[1]]
+        for h in handles:
+            rc = _lib.load().ffn_b200_set_launch_overlap(h, 1 if enable else 0)
+            if rc != _lib.OK:
+                raise ValueError(f"set_launch_overlap: {_lib.strerror(rc)}")
+        self.launch_overlap = bool(enable)
 
     def set_fault_injection(self, mode: int):
         """Test hook (1 = readiness waits can never be satisfied); see ffn_b200_set_fault_injection."""

@@ -278,6 +278,7 @@ struct ffn_b200_handle {
   Params params;
   unsigned epoch;
   unsigned epoch_limit;
+  int overlap;  // launch with programmatic stream serialisation (ffn_b200_set_launch_overlap)
 };
 
 extern "C" {
@@ -649,19 +650,31 @@ int ffn_b200_run(ffn_b200_handle* h, void* stream) {
   cfg.blockDim = dim3(static_cast<unsigned>(threads_for(h->plan.variant)), 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(h->plan.smem_bytes);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned n_attr = 0;
   if (h->plan.cta_pair) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-  } else {
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
+    attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+    attr[n_attr].val.clusterDim.x = 2;
+    attr[n_attr].val.clusterDim.y = 1;
+    attr[n_attr].val.clusterDim.z = 1;
+    ++n_attr;
+  } else if (!kVariants[h->plan.variant].rowblock && !h->overlap) {
+    // Row-block plans have no waits between CTAs: no co-residency needed.  An overlapped
+    // launch is a plain one too: a cooperative grid starts only once the previous grid has
+    // left every SM, which would void the overlap.  Its CTAs (one per SM, grid <= SMs) all
+    // become resident as the previous kernel's CTAs exit; the bounded waits report, rather
+    // than hang, if another stream's kernel kept SMs from them for longer than the limit.
+    attr[n_attr].id = cudaLaunchAttributeCooperative;
+    attr[n_attr].val.cooperative = 1;
+    ++n_attr;
+  }
+  if (h->overlap) {
+    attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attr;
   }
   cfg.attrs = attr;
-  // Row-block plans have no waits between CTAs: a plain launch, no co-residency needed.
-  cfg.numAttrs = kVariants[h->plan.variant].rowblock ? 0 : 1;
+  cfg.numAttrs = n_attr;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, h->kernel, h->params);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -790,6 +803,12 @@ int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, void* c
                             ffnb200::kStoreRows);
     if (e) return e;
   }
+  return FFN_B200_OK;
+}
+
+int ffn_b200_set_launch_overlap(ffn_b200_handle* h, int32_t enable) {
+  if (!h || (enable != 0 && enable != 1)) return FFN_B200_ERR_INVALID;
+  h->overlap = enable;
   return FFN_B200_OK;
 }
 

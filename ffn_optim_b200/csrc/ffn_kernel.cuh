@@ -188,6 +188,13 @@ __device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
 __device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation
+// may start while the previous kernel of the stream is finishing; `griddepcontrol.wait`
+// blocks until that kernel has completed and its memory is visible (it returns at once in a
+// kernel launched without the attribute).  `launch_dependents` lets the next such kernel be
+// scheduled (as SMs free up) before this one ends.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }
@@ -846,8 +853,6 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;
   const bool leader = rank == 0;
-  // Work-list owner (one per tile-sized group of CTAs).
-  const int cta = p.owner_map ? p.owner_map[blockIdx.x / kNcta] : static_cast<int>(blockIdx.x) / kNcta;
   const int slot_base = static_cast<int>(rank);          // partial / flag slot = (phase*C + cta)*kNcta + rank
 
   if (threadIdx.x == 0) {
@@ -901,6 +906,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
   if constexpr (PAIR) cluster_sync();  // peer barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touches on-chip state only; with an overlapped launch it runs while
+  // the previous kernel finishes.  Every global access (operands, hidden, counters, flags,
+  // partials, status) comes after this wait, so consecutive calls stay ordered.
+  if (threadIdx.x == 0) grid_dep_launch();
+  grid_dep_wait();
+  // Work-list owner (one per tile-sized group of CTAs).
+  const int cta = p.owner_map ? p.owner_map[blockIdx.x / kNcta] : static_cast<int>(blockIdx.x) / kNcta;
   if (threadIdx.x == 0) {
     trace_mark(p, kTrStart);
     if (p.trace) {
@@ -1388,16 +1400,20 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
       if (ew == 0 && lane == 0 && u.phase == 1 && !seen_down) trace_mark(p, kTrFirstDown);
       if (u.phase == 1) seen_down = true;
       // Stream-K owner: wait for every contributor's partial of this tile (same pair rank).
+      // Lane i acquires contributor c_first + i's flag, so the ~5 flags of a decode tile are
+      // polled at once rather than one L2 round trip after another; the warp barrier then
+      // orders every lane's reads of the partials after all of those acquires.
       if (u.role == kRoleOwner && u.c_first <= u.c_last) {
-        if (lane == 0) {
-          for (int c2 = u.c_first; c2 <= u.c_last && ok; ++c2)
-            ok = wait_word_ge(p.flags + (u.phase * p.C + c2) * kNcta + slot_base, EPI * p.epoch, abort_flag, p, 3,
-                              c2) ? 1 : 0;
+        for (int c0 = u.c_first; c0 <= u.c_last && ok; c0 += 32) {
+          const int c2 = c0 + lane;
+          int mine = 1;
+          if (c2 <= u.c_last)
+            mine = wait_word_ge(p.flags + (u.phase * p.C + c2) * kNcta + slot_base, EPI * p.epoch, abort_flag, p, 3,
+                                c2) ? 1 : 0;
+          ok = __all_sync(0xffffffffu, mine);
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __syncwarp();
         if (!ok) break;
-        for (int c2 = u.c_first; c2 <= u.c_last; ++c2)
-          (void)ld_acquire(p.flags + (u.phase * p.C + c2) * kNcta + slot_base);
       }
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * LY::kAccCols);
@@ -1418,17 +1434,16 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
           rs_push = rs_owner != p.rs_rank;
           rs_reduce = !rs_push;
           if (rs_reduce) {
+            // Lane `src` acquires rank src's flag (all ranks at once); the warp barrier orders
+            // every lane's reads of the staged partials after those acquires.
             const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
-            if (lane == 0) {
-              for (int src = 0; src < p.rs_world && ok; ++src)
-                if (src != p.rs_rank)
-                  ok = wait_word_ge<true>(p.rs_flags[p.rs_rank] + src * band + rs_tile, EPI * p.epoch, abort_flag,
-                                          p, 4, src) ? 1 : 0;
-            }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
+            int mine = 1;
+            if (lane < p.rs_world && lane != p.rs_rank)
+              mine = wait_word_ge<true>(p.rs_flags[p.rs_rank] + lane * band + rs_tile, EPI * p.epoch, abort_flag, p,
+                                        4, lane) ? 1 : 0;
+            ok = __all_sync(0xffffffffu, mine);
+            __syncwarp();
             if (!ok) break;
-            for (int src = 0; src < p.rs_world; ++src)
-              if (src != p.rs_rank) (void)ld_acquire_sys(p.rs_flags[p.rs_rank] + src * band + rs_tile);
           }
         }
       }
@@ -1588,13 +1603,31 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             continue;
           }
           if (u.role == kRoleOwner) {
+            // The contributors' partials, several float4 loads in flight (a decode tile has
+            // ~5 contributors: one L2 round trip per batch instead of one per contributor),
+            // added in contributor order as before, so the sum is the same bit for bit.  The
+            // fp8 tiles run 22 warps and have fewer registers per thread for the batch.
+            constexpr int kF4 = kCW / 4;
+            constexpr int kBatch = W8 ? (kF4 <= 2 ? 4 : 1) : 16 / kF4;
 #pragma unroll 1
-            for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
-              const float4* src = reinterpret_cast<const float4*>(ws_row(c2) + ch * kCW);
+            for (int c0 = u.c_first; c0 <= u.c_last; c0 += kBatch) {
+              float4 t[kBatch][kF4];
 #pragma unroll
-              for (int j = 0; j < kCW / 4; ++j) {
-                const float4 t = __ldcg(src + j);
-                v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+              for (int b = 0; b < kBatch; ++b) {
+                if (c0 + b <= u.c_last) {
+                  const float4* src = reinterpret_cast<const float4*>(ws_row(c0 + b) + ch * kCW);
+#pragma unroll
+                  for (int j = 0; j < kF4; ++j) t[b][j] = __ldcg(src + j);
+                }
+              }
+#pragma unroll
+              for (int b = 0; b < kBatch; ++b) {
+                if (c0 + b <= u.c_last) {
+#pragma unroll
+                  for (int j = 0; j < kF4; ++j) {
+                    v[4 * j] += t[b][j].x; v[4 * j + 1] += t[b][j].y; v[4 * j + 2] += t[b][j].z; v[4 * j + 3] += t[b][j].w;
+                  }
+                }
               }
             }
           }

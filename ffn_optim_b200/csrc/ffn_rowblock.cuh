@@ -111,6 +111,9 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // On-chip setup above; every global access below (overlapped launches, see grid_dep_wait).
+  if (threadIdx.x == 0) grid_dep_launch();
+  grid_dep_wait();
   if (threadIdx.x == 0) trace_mark(p, kTrStart);
 
   if (warp == 0) {

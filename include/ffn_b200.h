@@ -227,6 +227,15 @@ FFN_B200_EXPORT int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* handle,
 FFN_B200_EXPORT int ffn_b200_set_reduce_scatter(ffn_b200_handle* handle, int world, int rank, void* const* stage_ptrs,
                                                 void* const* flag_ptrs, void* y_local, int64_t ldy_local);
 
+/* Overlapped launches (programmatic dependent launch; off by default): with enable = 1,
+ * each later run lets its CTAs start, and set up their barriers and tensor memory, while
+ * the stream's previous kernel is still finishing; every global memory access of the
+ * kernel waits (griddepcontrol.wait) until that kernel has completed and its writes are
+ * visible, so results and stream order are those of serial launches.  Saves the launch gap
+ * and the setup of back-to-back calls (decode loops, CUDA graphs).  No counterpart in the
+ * reference. */
+FFN_B200_EXPORT int ffn_b200_set_launch_overlap(ffn_b200_handle* handle, int32_t enable);
+
 /* Tracing: when `device_stamps` (a device uint64[block_num][16], or NULL to switch off) is
  * set, every later run writes per-CTA %globaltimer stamps (ns): 0 setup done, 1 first TMA
  * load, 2 first down tile's hidden rows ready, 3 last load, 4 last MMA commit, 5 last up

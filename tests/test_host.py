@@ -307,3 +307,9 @@ def test_swiglu_packing_and_plan(lib):
         assert up == -(-rows // (128 if swap else info.tile_n))
     prob = _lib.Problem(16, 64, 520, 64, 1, 1, _lib.GELU_CODES["swiglu"], 0, 148)  # full_load_a
     assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_NOT_APPLICABLE
+
+
+def test_handle_setters_reject_null_and_bad_values(lib):
+    assert lib.ffn_b200_set_launch_overlap(None, 1) == _lib.ERR_INVALID
+    assert lib.ffn_b200_set_wait_limit(None, 1000) == _lib.ERR_INVALID
+    assert lib.ffn_b200_set_trace(None, None) == _lib.ERR_INVALID
