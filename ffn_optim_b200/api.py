@@ -23,7 +23,8 @@ class KernelCompilationError(RuntimeError):
 
 
 class EpochExhausted(RuntimeError):
-    """A reduce-scatter handle ran out of launch epochs; every rank must reset together."""
+    """Kept for API compatibility: the launch epoch lives on the device and no longer runs
+    out, so ``run`` does not raise it."""
 
 
 @dataclass
@@ -75,6 +76,29 @@ class PreparedFFN:
             if rc != _lib.OK:
                 raise RuntimeError(f"ffn_b200_run: {_lib.strerror(rc)}")
         return self._output_view()
+
+    def capture_graph(self, runs=1):
+        """Captures ``runs`` launches into a ``torch.cuda.CUDAGraph`` and returns it.
+
+        ``graph.replay()`` on the preparation stream then re-runs them: each reads X from
+        storage (``load_input`` or ``run(x)`` put it there) and writes the output view.  The
+        launch epoch lives on the device, so replays, eager runs and other graphs of this
+        FFN interleave freely; like runs, they must not overlap each other."""
+        import torch
+
+        if self.handle is None:
+            raise RuntimeError("PreparedFFN has been closed")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.device(self.storage[0].device):
+            side = torch.cuda.Stream()
+            side.wait_stream(self.stream)
+            with torch.cuda.graph(graph, stream=side):
+                for _ in range(runs):
+                    rc = _lib.load().ffn_b200_run(self.handle, ctypes.c_void_p(side.cuda_stream))
+                    if rc != _lib.OK:
+                        raise RuntimeError(f"ffn_b200_run (capture): {_lib.strerror(rc)}")
+            self.stream.wait_stream(side)
+        return graph
 
     def _chunk_handles(self, chunks):
         """Launch handles for M-chunks of this FFN (rows rounded to 128), sharing its storage:

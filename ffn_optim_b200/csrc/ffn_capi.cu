@@ -276,8 +276,6 @@ struct ffn_b200_handle {
   int device;
   KernelFn kernel;
   Params params;
-  unsigned epoch;
-  unsigned epoch_limit;
   int overlap;  // launch with programmatic stream serialisation (ffn_b200_set_launch_overlap)
 };
 
@@ -295,7 +293,7 @@ const char* ffn_b200_strerror(int code) {
     case FFN_B200_ERR_CUDA: return "CUDA call failed";
     case FFN_B200_ERR_ALIGNMENT: return "buffer base not 16-byte aligned or pitch not a multiple of 8 elements";
     case FFN_B200_ERR_TOO_LARGE: return "problem does not fit one launch";
-    case FFN_B200_ERR_EPOCH: return "launch epoch exhausted: reset every rank of the reduce-scatter together";
+    case FFN_B200_ERR_EPOCH: return "launch epoch exhausted (not returned: the epoch lives on the device)";
     case FFN_B200_ERR_SCRATCH:
       return "problem needs more scratch than the 32 MiB that ffn_b200_run_noalloc holds; use ffn_b200_prepare";
   }
@@ -488,7 +486,6 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   h->buf = *b;
   h->device = device;
   h->kernel = kernel_for(plan.variant, prob.dtype == FFN_B200_BF16, prob.gelu);
-  h->epoch = 0;
 
   Params& P = h->params;
   std::memset(&P, 0, sizeof(P));
@@ -541,6 +538,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.ldy = b->ldy;
   P.ws = b->workspace;
   P.claims = reinterpret_cast<unsigned long long*>(b->counters);
+  P.launches = reinterpret_cast<unsigned long long*>(b->counters + 4);
   P.counters = b->counters + ffnb200::kClaimWords;
   P.dyn = plan.schedule == 2 ? 1 : 0;
   P.flags = b->flags;
@@ -562,9 +560,9 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
   P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : (prob.l2_policy == 4 ? 3 : 0));
-  // Readiness counters gain epi * ncta * (up tiles per row block) per launch, flags epi per launch.
-  const int64_t per_blk = static_cast<int64_t>(kVariants[plan.variant].epi) * ncta * (sw ? plan.up.tiles_r : plan.up.tiles_q);
-  h->epoch_limit = static_cast<unsigned>(((int64_t(1) << 30) / (per_blk > 4 ? per_blk : 4)));
+  // The launch epoch lives on the device (Params::launches, in the counters buffer): readiness
+  // counters gain epi * ncta * (up tiles per row block) per launch and flags epi per launch,
+  // compared modulo 2^32, so nothing here counts launches and a captured launch replays.
 
   int cur = 0;
   cudaGetDevice(&cur);
@@ -627,23 +625,12 @@ int ffn_b200_reset(ffn_b200_handle* h, void* stream) {
       return FFN_B200_ERR_CUDA;
     }
   }
-  h->epoch = 0;
   return FFN_B200_OK;
 }
 
 int ffn_b200_run(ffn_b200_handle* h, void* stream) {
   if (!h) return FFN_B200_ERR_INVALID;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (h->epoch + 1 >= h->epoch_limit) {
-    // Under the fused reduce-scatter the counts live partly in other GPUs' memory: all ranks
-    // must reset together at a quiescent point, so the caller is told instead.
-    if (h->params.rs_world > 1) return FFN_B200_ERR_EPOCH;
-    const int rc = ffn_b200_reset(h, stream);
-    if (rc) return rc;
-  }
-  h->epoch += 1;
-  h->params.epoch = h->epoch;
-
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(static_cast<unsigned>(h->plan.block_num), 1, 1);
@@ -678,7 +665,6 @@ int ffn_b200_run(ffn_b200_handle* h, void* stream) {
   const cudaError_t e = cudaLaunchKernelEx(&cfg, h->kernel, h->params);
   if (e != cudaSuccess) {
     cudaGetLastError();
-    h->epoch -= 1;
     return FFN_B200_ERR_CUDA;
   }
   return FFN_B200_OK;

@@ -75,7 +75,11 @@ struct Params {
   PhaseSched up, dn;
   int M, H, N;
   int C;
-  unsigned epoch;
+  // Launch epoch, kept on the device so that a launch captured in a CUDA graph replays
+  // correctly: every CTA adds 1 to `launches` (a u64 that only a reset zeroes), so the CTAs
+  // of launch e read (e-1)*grid .. e*grid-1 and all compute e = old / grid + 1.  Counters and
+  // flags grow by a fixed amount per launch; their waits compare modulo 2^32 against e.
+  unsigned long long* launches;
   unsigned long long wait_limit_ns;
   int inject;
   int l2_hints;          // 1: evict-last on A (row operand), evict-first on B; 2: evict-normal on
@@ -103,8 +107,9 @@ struct Params {
 
 static_assert(sizeof(Params) <= 4096, "kernel parameters must fit the 4 KB parameter space");
 
-// u32 words at the start of the counters buffer that hold the two u64 tile-claim counters.
-constexpr int kClaimWords = 4;
+// u32 words at the start of the counters buffer: the two u64 tile-claim counters, then the
+// u64 launch counter (Params::launches).
+constexpr int kClaimWords = 6;
 
 // Per-CTA trace stamps (ns, %globaltimer) written when Params::trace is set.
 enum TraceSlot : int {
@@ -793,7 +798,9 @@ struct Layout {
   static_assert(kChains <= 4 * KSUB, "every chain gets a K step from each k-block");
   static_assert(!W8 || (kQSlots >= STAGES + kCvtGroups + 1 && kCvtGroups <= STAGES), "ring depths");
   static_assert((kBSub % 1024) == 0, "B tile must be whole swizzle atoms");
-  static_assert((W8 ? 2 * STAGES + 6 + 2 * kQSlots + 2 * kBSlots : 2 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");
+  // (the last 16 bytes hold the epoch barrier and the launch epoch)
+  static_assert((W8 ? 2 * STAGES + 6 + 2 * kQSlots + 2 * kBSlots : 2 * STAGES + 5) * 8 + 8 <= kBarBytes - 16,
+                "barrier area");
   static_assert(!W8 || (SWAP && !PAIR && (KSUB == 1 || KSUB == 2)), "fp8 weights: swap-AB decode tiles");
   static_assert(!PAIR || !SWAP, "CTA pairs are used for prefill tiles only");
   static_assert(EPI == 4 || EPI == 8, "epilogue warps: one or two per TMEM sub-partition");
@@ -838,6 +845,16 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
   const uint32_t drain_bar = sBar + 8u * (2 * STAGES + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (sBar - base) + 8 * (2 * STAGES + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // The launch epoch: published once by the first epilogue warp (one atomic per CTA), read
+  // by the roles that wait on counters or flags when they first need it.
+  const uint32_t epoch_bar = sBar + LY::kBarBytes - 16;
+  volatile unsigned long long* epoch_val =
+      reinterpret_cast<volatile unsigned long long*>(gbase + (sBar - base) + LY::kBarBytes - 8);
+  auto fetch_epoch = [&](unsigned long long& e) -> bool {
+    if (!wait_bar(epoch_bar, 0u, abort_flag, p, 700)) return false;
+    e = *epoch_val;
+    return true;
+  };
   const uint32_t sRing = sBar + LY::kBarBytes;
   const uint32_t sQ = sBar + LY::kQOffset;      // fp8 weight k-blocks (W8), 1024-aligned
   const uint32_t sBR = sBar + LY::kBRingOffset;  // token-operand k-blocks (W8), 1024-aligned
@@ -879,6 +896,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
       mbar_init(tempty_bar(a), 32 * EPI * kNcta);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(epoch_bar, 1);
 #pragma unroll 1
     for (int i = 0; i < LY::kRing; ++i) {
       mbar_init(ring_full(i), 1);
@@ -930,7 +948,16 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
       long long issued = 0;
       int ready_blk = -1;
       const unsigned per_blk = static_cast<unsigned>(EPI * kNcta) * static_cast<unsigned>(SWAP ? p.up.tiles_r : p.up.tiles_q);
-      const unsigned target = p.epoch * per_blk + (p.inject ? 1u : 0u);
+      unsigned long long epoch = 0;  // fetched when first needed (readiness waits, claims)
+      unsigned target = 0;
+      bool have_epoch = false;
+      auto need_epoch = [&]() -> bool {
+        if (have_epoch) return true;
+        if (!fetch_epoch(epoch)) return false;
+        target = static_cast<unsigned>(epoch) * per_blk + (p.inject ? 1u : 0u);
+        have_epoch = true;
+        return true;
+      };
       // Optional L2 policy (off by default: on cfg5 it raised DRAM reads from 62 GB to 430 GB).
       const uint64_t pol_a = p.l2_hints == 2 ? policy_evict_normal() : policy_evict_last();
       const uint64_t pol_b = p.l2_hints == 2 ? policy_evict_normal() : policy_evict_first();
@@ -959,7 +986,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             const uint32_t bpar = static_cast<uint32_t>((issued / LY::kBSlots) & 1);
             if (!wait_bar(bempty_bar(jb), bpar ^ 1u, abort_flag, p, 170 + jb)) return false;
             if (u.phase == 1 && tq != ready_blk) {  // swap mode: the row block is a token block
-              if (!wait_word_ge(p.counters + tq, target, abort_flag, p, 2, tq)) return false;
+              if (!need_epoch() || !wait_word_ge(p.counters + tq, target, abort_flag, p, 2, tq)) return false;
               fence_async_global();
               if (ready_blk < 0) trace_mark(p, kTrDownReady);
               ready_blk = tq;
@@ -1022,7 +1049,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
               ++issued;
               if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
-            if (!wait_word_ge(p.counters + blk, target, abort_flag, p, 2, blk)) return false;
+            if (!need_epoch() || !wait_word_ge(p.counters + blk, target, abort_flag, p, 2, blk)) return false;
             fence_async_global();
             if (ready_blk < 0) trace_mark(p, kTrDownReady);
             ready_blk = blk;
@@ -1068,13 +1095,16 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
           // Every owner ends with one failed claim, so each launch advances the counter by
           // exactly max(dp - C, 0) + C.  The next claim is in flight during the loads.
           const long long span = max(s.dp - p.C, 0) + p.C;
-          const unsigned long long base = static_cast<unsigned long long>(p.epoch - 1u) * span;
           const long long t_end = max(s.dp, p.C) + p.C;  // claimed tiles lie in [C, t_end)
-          auto claimed = [&](unsigned long long raw) { return p.C + static_cast<long long>(raw - base); };
+          auto claimed = [&](unsigned long long raw) {  // (after need_epoch)
+            return p.C + static_cast<long long>(raw - (epoch - 1ull) * static_cast<unsigned long long>(span));
+          };
           long long t = cta;
           bool from_claim = false;
           if (p.dyn && t >= s.dp) {
-            t = claimed(atomicAdd(p.claims + ph, 1ull));
+            const unsigned long long raw = atomicAdd(p.claims + ph, 1ull);
+            if (!need_epoch()) { ok = false; break; }
+            t = claimed(raw);
             from_claim = true;
           }
 #pragma unroll 1
@@ -1095,6 +1125,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             if (p.dyn) next = atomicAdd(p.claims + ph, 1ull);
             if (!do_loads(u)) { ok = false; break; }
             if (p.dyn) {
+              if (!need_epoch()) { ok = false; break; }
               t = claimed(next);
               from_claim = true;
             } else {
@@ -1367,6 +1398,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
     uint32_t acc_phase = 0;
     int sbuf = 0;
     bool seen_down = false;
+    if (ew == 0 && lane == 0) {  // this CTA's share of the launch count -> the launch epoch
+      const unsigned long long old = atomicAdd(p.launches, 1ull);
+      *epoch_val = old / gridDim.x + 1ull;
+      mbar_arrive(epoch_bar);
+    }
+    unsigned long long epoch = 0;  // fetched before the first flag wait or staging slot
+    bool have_epoch = false;
 #pragma unroll 1
     for (int seq = 0;; ++seq) {
       // Next unit from the ring: lane 0 waits, the warp reads the slot, lane 0 frees it.
@@ -1399,6 +1437,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
       tc_fence_after();
       if (ew == 0 && lane == 0 && u.phase == 1 && !seen_down) trace_mark(p, kTrFirstDown);
       if (u.phase == 1) seen_down = true;
+      if (!have_epoch && (u.role == kRoleOwner || p.rs_world > 1)) {
+        if (lane == 0) ok = fetch_epoch(epoch) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        epoch = __shfl_sync(0xffffffffu, epoch, 0);
+        have_epoch = true;
+      }
       // Stream-K owner: wait for every contributor's partial of this tile (same pair rank).
       // Lane i acquires contributor c_first + i's flag, so the ~5 flags of a decode tile are
       // polled at once rather than one L2 round trip after another; the warp barrier then
@@ -1408,8 +1453,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
           const int c2 = c0 + lane;
           int mine = 1;
           if (c2 <= u.c_last)
-            mine = wait_word_ge(p.flags + (u.phase * p.C + c2) * kNcta + slot_base, EPI * p.epoch, abort_flag, p, 3,
-                                c2) ? 1 : 0;
+            mine = wait_word_ge(p.flags + (u.phase * p.C + c2) * kNcta + slot_base,
+                                EPI * static_cast<unsigned>(epoch), abort_flag, p, 3, c2) ? 1 : 0;
           ok = __all_sync(0xffffffffu, mine);
         }
         __syncwarp();
@@ -1439,8 +1484,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
             int mine = 1;
             if (lane < p.rs_world && lane != p.rs_rank)
-              mine = wait_word_ge<true>(p.rs_flags[p.rs_rank] + lane * band + rs_tile, EPI * p.epoch, abort_flag, p,
-                                        4, lane) ? 1 : 0;
+              mine = wait_word_ge<true>(p.rs_flags[p.rs_rank] + lane * band + rs_tile,
+                                        EPI * static_cast<unsigned>(epoch), abort_flag, p, 4, lane) ? 1 : 0;
             ok = __all_sync(0xffffffffu, mine);
             __syncwarp();
             if (!ok) break;
@@ -1449,7 +1494,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
       }
       auto rs_slot = [&](int dst_rank, int src) {  // this thread's row of a staging slot
         const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
-        const size_t slot = ((static_cast<size_t>(p.epoch & 1u) * p.rs_world + src) * band + rs_tile) * kBM + row;
+        const size_t slot = ((static_cast<size_t>(epoch & 1u) * p.rs_world + src) * band + rs_tile) * kBM + row;
         return p.rs_stage[dst_rank] + slot * BN;
       };
 
@@ -1567,7 +1612,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
               // The owner's staging slot (this rank's partial of the tile): one 4 KB bulk
               // store over NVLink per chunk and warp.
               const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
-              const int srow = static_cast<int>(((static_cast<size_t>(p.epoch & 1u) * p.rs_world + p.rs_rank) * band +
+              const int srow = static_cast<int>(((static_cast<size_t>(epoch & 1u) * p.rs_world + p.rs_rank) * band +
                                                  rs_tile) * kBM) + sub * 32;
               tma_store_2d(&p.tm_rs[rs_owner], sb, ch * 64, srow);
             } else {

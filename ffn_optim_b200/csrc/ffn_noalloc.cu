@@ -160,6 +160,7 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   P.ldy = ldy;
   P.ws = ws;
   P.claims = reinterpret_cast<unsigned long long*>(counters);
+  P.launches = reinterpret_cast<unsigned long long*>(counters + 4);
   P.counters = counters + ffnb200::kClaimWords;
   P.dyn = plan.schedule == 2 ? 1 : 0;
   P.flags = flags;
@@ -170,7 +171,6 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   P.H = static_cast<int>(prob.h);
   P.N = static_cast<int>(prob.n);
   P.C = plan.block_num;
-  P.epoch = 1;
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
   P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : (prob.l2_policy == 4 ? 3 : 0));

@@ -48,7 +48,7 @@ typedef enum {
   FFN_B200_ERR_ALIGNMENT = 6,      /* base not 16-byte aligned or pitch not a multiple of 8 elements */
   FFN_B200_ERR_TOO_LARGE = 7,      /* tile count does not fit one launch */
   FFN_B200_ERR_SCRATCH = 8,        /* needs more scratch than ffn_b200_run_noalloc holds */
-  FFN_B200_ERR_EPOCH = 9           /* reduce-scatter handle needs a collective reset (after ~2^30/tiles runs) */
+  FFN_B200_ERR_EPOCH = 9           /* kept for ABI stability; no longer returned (the launch epoch lives on the device) */
 } ffn_b200_status;
 
 typedef enum { FFN_B200_F16 = 0, FFN_B200_BF16 = 1 } ffn_b200_dtype;
@@ -178,13 +178,14 @@ FFN_B200_EXPORT int ffn_b200_device_info(int device, int* sm_count, int* cc_majo
 FFN_B200_EXPORT int ffn_b200_make_plan(const ffn_b200_problem* problem, ffn_b200_plan* plan);
 
 /* Validates device and buffers, encodes the TMA tensor maps and returns a handle that
- * launches one fused kernel per ffn_b200_run.  The handle keeps a launch epoch so the
- * readiness counters never need clearing between runs. */
+ * launches one fused kernel per ffn_b200_run.  The launch epoch lives on the device (a
+ * 64-bit launch count at the start of `counters`), so the readiness counters never need
+ * clearing between runs and a run captured in a CUDA graph replays any number of times. */
 FFN_B200_EXPORT int ffn_b200_prepare(const ffn_b200_problem* problem, const ffn_b200_buffers* buffers,
                      int device, ffn_b200_handle** handle);
 
-/* One asynchronous launch on `stream` (a cudaStream_t).  Runs of one handle must be
- * serialised on one stream. */
+/* One asynchronous launch on `stream` (a cudaStream_t; may be capturing into a CUDA graph).
+ * Runs of one handle must be serialised on one stream (graph replays included). */
 FFN_B200_EXPORT int ffn_b200_run(ffn_b200_handle* handle, void* stream);
 
 /* Re-points X and Y of a prepared handle (same shapes and pitches) without re-planning. */
