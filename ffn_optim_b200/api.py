@@ -378,7 +378,9 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
     bytes, a weight-quantization error on top of the reference arithmetic.  Storage copies
     are device work timed separately as ``preparation['auxiliary_device_interval_ms']``.
 
-    Beyond the reference's V1: ``activation='silu'`` replaces the GELU by SiLU;
+    Beyond the reference's V1: ``layout='canonical'`` takes W1 as [K, H] and W2 as [H, N]
+    (``Y = GELU(X W1) W2``), copied once into Linear storage; ``activation='silu'`` replaces
+    the GELU by SiLU;
     ``activation='swiglu'`` takes ``weight1 = [W_gate; W_up]`` ([2H, K]) and computes
     ``hidden = SiLU(x W_gate^T) * (x W_up^T)``; ``bias1`` [H] / ``bias2`` [N] (input dtype) are
     added to the fp32 sums before the activation / before the final rounding (``bias1`` not
@@ -391,6 +393,16 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
     if gelu not in ("rational", "erf"):
         raise ValueError("gelu must be 'rational' or 'erf'")
     glu = activation == "swiglu"
+    canonical = layout == "canonical"
+    if canonical:
+        # Canonical weights (W1 [K, H], W2 [H, N], X @ W1 without a transpose) are the same
+        # weights stored transposed: validated and planned as their Linear views, then copied
+        # once into Linear storage with the other preparation copies.
+        if glu:
+            raise ValueError("activation='swiglu' takes Linear weights (gate and up as row halves of weight1)")
+        if not all(isinstance(w, torch.Tensor) and w.dim() == 2 for w in (weight1, weight2)):
+            raise ValueError("layout='canonical' takes 2-D weight1 [K, H] and weight2 [H, N]")
+        weight1, weight2, layout = weight1.t(), weight2.t(), "linear"
     if glu:
         # W1 = [gate rows; up rows], [2H, K]; validated as the gate half against W2 [N, H]
         if not isinstance(weight1, torch.Tensor) or weight1.dim() != 2 or isinstance(weight2, torch.Tensor) and (
@@ -421,6 +433,8 @@ def prepare_ffn(x, weight1, weight2, *, up_impl="basic", down_impl="basic", bloc
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         scales = None
+        if canonical:
+            weight1, weight2 = weight1.contiguous(), weight2.contiguous()
         if glu:  # the kernel's gate/up row order
             weight1 = pack_swiglu(weight1, p.h, plan.kernel["swap_ab"])
         if weight_format == "fp8":

@@ -313,3 +313,15 @@ def test_handle_setters_reject_null_and_bad_values(lib):
     assert lib.ffn_b200_set_launch_overlap(None, 1) == _lib.ERR_INVALID
     assert lib.ffn_b200_set_wait_limit(None, 1000) == _lib.ERR_INVALID
     assert lib.ffn_b200_set_trace(None, None) == _lib.ERR_INVALID
+
+
+def test_canonical_layout_rules_on_host():
+    """The shape contract keeps the reference's V1 rule (Linear only); prepare_ffn accepts
+    Canonical weights by transposing them, but not with SwiGLU (gate/up are row halves)."""
+    from ffn_optim_b200 import prepare_ffn
+
+    with pytest.raises(ValueError):
+        problem_from_shapes((4, 8), (8, 16), (16, 4), layout="canonical")
+    x, w1, w2 = torch.zeros(4, 8), torch.zeros(8, 32), torch.zeros(16, 4)
+    with pytest.raises(ValueError, match="swiglu"):
+        prepare_ffn(x, w1, w2, layout="canonical", activation="swiglu")
