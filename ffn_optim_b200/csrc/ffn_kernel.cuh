@@ -1462,10 +1462,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
       }
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * LY::kAccCols);
-      auto ws_row = [&](int c) {
-        return p.ws + (static_cast<size_t>((u.phase * p.C + c) * kNcta + slot_base) * kBM + row) * BN;
+      // Stream-K partial slot of CTA c (kBM x BN fp32), stored as [BN/4 column groups][kBM rows]
+      // float4: the 32 lanes of a warp (consecutive rows) write and read 512 contiguous bytes
+      // per access.  This thread's float4 of column group g:
+      auto ws_f4 = [&](int c, int g) {
+        return reinterpret_cast<float4*>(p.ws) +
+               (static_cast<size_t>((u.phase * p.C + c) * kNcta + slot_base) * (BN / 4) + g) * kBM + row;
       };
-      float* ws_own = ws_row(cta);
 
       // Fused reduce-scatter (down phase, tile finalised here): push to the owning rank, or
       // (own band) wait for every other rank's partial of this tile.
@@ -1512,18 +1515,17 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
           tmem_ld32(tbase + ch * 64, v);
           tmem_ld32(tbase + ch * 64 + 32, v + 32);
           if (u.role == kRoleContrib) {
-            float4* dst = reinterpret_cast<float4*>(ws_own + ch * 64);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int j = 0; j < 16; ++j)
+              *ws_f4(cta, ch * 16 + j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             continue;
           }
           if (u.role == kRoleOwner) {
 #pragma unroll 1
             for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
-              const float4* src = reinterpret_cast<const float4*>(ws_row(c2) + ch * 64);
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                const float4 t = __ldcg(src + j);
+                const float4 t = __ldcg(ws_f4(c2, ch * 16 + j));
                 v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
               }
             }
@@ -1540,10 +1542,9 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
                 if (u.role == kRoleOwner) {
 #pragma unroll 1
                   for (int c2 = u.c_first; c2 <= u.c_last; ++c2) {
-                    const float4* src = reinterpret_cast<const float4*>(ws_row(c2) + (ch + 1) * 64 + hh * 32);
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                      const float4 t = __ldcg(src + j);
+                      const float4 t = __ldcg(ws_f4(c2, (ch + 1) * 16 + hh * 8 + j));
                       w[4 * j] += t.x; w[4 * j + 1] += t.y; w[4 * j + 2] += t.z; w[4 * j + 3] += t.w;
                     }
                   }
@@ -1642,9 +1643,9 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             for (int j = 0; j < kCW; ++j) v[j] += w[j];
           }
           if (u.role == kRoleContrib) {
-            float4* dst = reinterpret_cast<float4*>(ws_own + ch * kCW);
 #pragma unroll
-            for (int j = 0; j < kCW / 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int j = 0; j < kCW / 4; ++j)
+              *ws_f4(cta, ch * (kCW / 4) + j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             continue;
           }
           if (u.role == kRoleOwner) {
@@ -1660,9 +1661,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
 #pragma unroll
               for (int b = 0; b < kBatch; ++b) {
                 if (c0 + b <= u.c_last) {
-                  const float4* src = reinterpret_cast<const float4*>(ws_row(c0 + b) + ch * kCW);
 #pragma unroll
-                  for (int j = 0; j < kF4; ++j) t[b][j] = __ldcg(src + j);
+                  for (int j = 0; j < kF4; ++j) t[b][j] = __ldcg(ws_f4(c0 + b, ch * kF4 + j));
                 }
               }
 #pragma unroll
