@@ -134,3 +134,32 @@ def test_fp8_row_quantization_and_ffn():
     ref = O.from_bits(O.ffn(x, O.E4M3_VALUES[q] * s[:, None], O.E4M3_VALUES[q2] * s2[:, None], "bfloat16",
                             staged=True, rational=True), "bfloat16")
     assert np.abs(got - ref).max() <= 2 ** -6 * np.abs(ref).max()
+
+
+def test_epilogue_extensions_match_torch_fp32():
+    """The oracle's build extensions (biases, SiLU, SwiGLU; no reference counterpart) against
+    torch's own fp32 definitions on the same inputs: hidden rounded to the dtype once, Y
+    rounded once."""
+    import torch
+
+    g = np.random.default_rng(7)
+    m, k, h, n = 9, 24, 40, 12
+    x = g.standard_normal((m, k)).astype(np.float32)
+    w1 = (g.standard_normal((2 * h, k)) * 0.2).astype(np.float32)
+    w2 = (g.standard_normal((n, h)) * 0.2).astype(np.float32)
+    b1 = g.standard_normal(h).astype(np.float32)
+    b2 = g.standard_normal(n).astype(np.float32)
+    t = lambda a: torch.from_numpy(a)  # noqa: E731
+    for dt, tdt in (("bfloat16", torch.bfloat16), ("float16", torch.float16)):
+        z = t(x) @ t(w1[:h]).T + t(b1)
+        hid = torch.nn.functional.silu(z).to(tdt).float()
+        ref = (hid @ t(w2).T + t(b2)).to(tdt)
+        got = O.ffn(x, w1[:h], w2, dt, staged=True, b1=b1, b2=b2, activation="silu")
+        diff = O.ulp_distance(got, ref.view(torch.int16).numpy().view(np.uint16))
+        assert diff.max() <= 2, dt
+        zz = t(x) @ t(w1).T
+        hid = (torch.nn.functional.silu(zz[:, :h]) * zz[:, h:]).to(tdt).float()
+        ref = (hid @ t(w2).T).to(tdt)
+        got = O.ffn(x, w1, w2, dt, staged=True, activation="swiglu")
+        diff = O.ulp_distance(got, ref.view(torch.int16).numpy().view(np.uint16))
+        assert diff.max() <= 2, dt
