@@ -75,7 +75,7 @@ class PlanInfo(ctypes.Structure):
                 ("block_num", ctypes.c_int32), ("tmem_cols", ctypes.c_int32), ("smem_bytes", ctypes.c_int64),
                 ("up", PhasePlan), ("down", PhasePlan), ("workspace_floats", ctypes.c_int64),
                 ("counter_words", ctypes.c_int64), ("flag_words", ctypes.c_int64),
-                ("status_words", ctypes.c_int64), ("schedule", ctypes.c_int32)]
+                ("status_words", ctypes.c_int64), ("schedule", ctypes.c_int32), ("row_split", ctypes.c_int32)]
 
     def to_dict(self):
         out = {}

@@ -184,7 +184,11 @@ int plan_rowblock(const ffn_b200_problem& pr, int grid, ffn_b200_plan* out) {
   const int64_t rows = cdiv(pr.m, ffnb200::kBM);
   const int64_t chunks = cdiv(pr.h, 128);
   if (rows * chunks >= (int64_t(1) << 31)) return FFN_B200_ERR_TOO_LARGE;
-  const int C = static_cast<int>(rows < grid ? rows : grid);
+  // Few row blocks: clusters of S CTAs split each block's H chunks (S = 2 or 4 while S*rows
+  // CTAs fit the grid and every CTA keeps at least one chunk); one row block per cluster.
+  int S = 1;
+  while (S < 4 && rows * S * 2 <= grid && chunks >= S * 2) S *= 2;
+  const int C = static_cast<int>(S > 1 ? rows * S : (rows < grid ? rows : grid));
   auto fill = [&](ffn_b200_phase_plan* ph, int64_t tq, int64_t depth) {
     ph->tiles_r = static_cast<int32_t>(rows);
     ph->tiles_q = static_cast<int32_t>(tq);
@@ -208,6 +212,7 @@ int plan_rowblock(const ffn_b200_problem& pr, int grid, ffn_b200_plan* out) {
   out->flag_words = 2;
   out->status_words = 4;
   out->schedule = 1;
+  out->row_split = S;
   return FFN_B200_OK;
 }
 
@@ -433,6 +438,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   // and little drift (cfg5: 52 GB static against 64 GB dynamic) and for decode grids of one
   // or two waves, where a claim would only add its latency.
   out->schedule = pr->schedule ? pr->schedule : (v.pair ? 2 : 1);
+  out->row_split = 1;
   return FFN_B200_OK;
 }
 
@@ -557,6 +563,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   P.N = static_cast<int>(prob.n);
   const int ncta = plan.cta_pair ? 2 : 1;
   P.C = plan.block_num / ncta;
+  P.rb_split = plan.row_split;
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
   P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : (prob.l2_policy == 4 ? 3 : 0));
@@ -639,9 +646,9 @@ int ffn_b200_run(ffn_b200_handle* h, void* stream) {
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   unsigned n_attr = 0;
-  if (h->plan.cta_pair) {
+  if (h->plan.cta_pair || h->plan.row_split > 1) {  // CTA pairs; split row blocks
     attr[n_attr].id = cudaLaunchAttributeClusterDimension;
-    attr[n_attr].val.clusterDim.x = 2;
+    attr[n_attr].val.clusterDim.x = h->plan.cta_pair ? 2 : static_cast<unsigned>(h->plan.row_split);
     attr[n_attr].val.clusterDim.y = 1;
     attr[n_attr].val.clusterDim.z = 1;
     ++n_attr;

@@ -99,6 +99,7 @@ struct Params {
   // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
   // of another rank's band is pushed as a bf16 partial into that rank's staging buffer over
   // NVLink; an owner sums the partials of its band in ascending rank order.
+  int rb_split;          // row-block kernel: CTAs (a cluster) sharing one row block's H chunks
   int rs_world, rs_rank, rs_band_tiles;
   uint16_t* rs_stage[kMaxRanks];   // per rank: [2 parity][world][band tiles][kBM][BN] bf16
   unsigned* rs_flags[kMaxRanks];   // per rank: [world][band tiles] push counts (4 per launch)
@@ -316,6 +317,14 @@ __device__ __forceinline__ void st_shared_8(uint32_t addr, const int* v) {
                : "memory");
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr + 16), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
 }
 __device__ __forceinline__ void st_cluster_8(uint32_t cluster_addr, const int* v) {
   asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v[0]), "r"(v[1]),

@@ -167,6 +167,7 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   P.status = st;
   P.up = to_sched(plan.up);
   P.dn = to_sched(plan.down);
+  P.rb_split = plan.row_split;
   P.M = static_cast<int>(prob.m);
   P.H = static_cast<int>(prob.h);
   P.N = static_cast<int>(prob.n);
@@ -196,8 +197,15 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   cfg.dynamicSmemBytes = static_cast<size_t>(plan.smem_bytes);
   cfg.stream = sh;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  if (rowblock && plan.row_split > 1) {  // a cluster per split row block
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(plan.row_split);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kernel, P) != cudaSuccess) {

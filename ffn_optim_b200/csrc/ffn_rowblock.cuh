@@ -21,6 +21,13 @@
 // sum, hidden rounded once to the input dtype, fp32 accumulation over H, one rounding of
 // Y.  Only the order of the H summation differs (chunks of 128 in ascending order, inside
 // one accumulator).
+//
+// Few row blocks (M <= 128 * SMs / 2): a cluster of S = Params::rb_split CTAs shares each
+// row block, CTA s taking H chunks [s*J/S, (s+1)*J/S), so S times as many SMs work and
+// each walks 1/S of the chain.  At the end every CTA s > 0 leaves its fp32 Y partial in its
+// own (then idle) operand ring; after a cluster barrier CTA 0 reads them over distributed
+// shared memory and adds them to its accumulator in rank order (fixed, so the result is
+// the same on every run), and a second barrier keeps the peers resident until it has read.
 #pragma once
 
 #include "ffn_kernel.cuh"
@@ -41,6 +48,8 @@ struct RowLayout {
   static_assert(NY * kBK * 2 <= kStage, "W2 k-block fits a stage");
   static_assert((2 * STAGES + 12) * 8 + 8 <= kBarBytes, "barrier area");
   static_assert(kSmem <= 232448, "dynamic shared memory per CTA");
+  // A split row block's Y partial (kBM x 256 fp32) lives in the operand ring at the end.
+  static_assert(STAGES * kStage >= kBM * 256 * 4, "Y partial fits the operand ring");
 };
 
 template <int NY, int STAGES, bool BF16, int GELU>
@@ -76,6 +85,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
   const int RB = p.up.tiles_r;   // row blocks
   const int J = p.up.tiles_q;    // H chunks
   const int KB = p.up.L;         // 64-wide k-blocks of K
+  // H split: CTA `srank` of a cluster of S takes chunks [j0, j0 + Js) of its row block.
+  const int S = p.rb_split > 1 ? p.rb_split : 1;
+  const int srank = S > 1 ? static_cast<int>(cluster_rank()) : 0;
+  const int j0 = srank * J / S;
+  const int Js = (srank + 1) * J / S - j0;
+  const int rb_first = static_cast<int>(blockIdx.x) / S;
+  const int rb_step = static_cast<int>(gridDim.x) / S;
 
   if (threadIdx.x == 0) {
 #pragma unroll 1
@@ -132,10 +148,11 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       };
 #pragma unroll 1
-      for (int rb = blockIdx.x; rb < RB && ok; rb += gridDim.x) {
+      for (int rb = rb_first; rb < RB && ok; rb += rb_step) {
 #pragma unroll 1
-        for (int j = 0; j <= J && ok; ++j) {
-          if (j < J) {  // up(j): X and W1 k-blocks
+        for (int jj = 0; jj <= Js && ok; ++jj) {
+          const int j = j0 + jj;
+          if (jj < Js) {  // up(j): X and W1 k-blocks
 #pragma unroll 1
             for (int kb = 0; kb < KB; ++kb) {
               if (!next_stage()) { ok = false; break; }
@@ -147,7 +164,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
               advance();
             }
           }
-          if (ok && j >= 1) {  // down(j-1): the two W2 k-blocks of chunk j-1
+          if (ok && jj >= 1) {  // down(j-1): the two W2 k-blocks of chunk j-1
 #pragma unroll 1
             for (int kk = 0; kk < 2; ++kk) {
               if (!next_stage()) { ok = false; break; }
@@ -224,11 +241,11 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         return true;
       };
 #pragma unroll 1
-      for (int rb = blockIdx.x; rb < RB && ok; rb += gridDim.x) {
+      for (int rb = rb_first; rb < RB && ok; rb += rb_step) {
 #pragma unroll 1
-        for (int j = 0; j <= J && ok; ++j) {
-          if (j < J && !up_chunk()) ok = false;
-          if (ok && j >= 1 && !down_chunk(j == 1)) ok = false;
+        for (int jj = 0; jj <= Js && ok; ++jj) {
+          if (jj < Js && !up_chunk()) ok = false;
+          if (ok && jj >= 1 && !down_chunk(jj == 1)) ok = false;
         }
         if (!ok) break;
         umma_commit(yfull);
@@ -276,9 +293,10 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
       }
     };
 #pragma unroll 1
-    for (int rb = blockIdx.x; rb < RB && ok; rb += gridDim.x) {
+    for (int rb = rb_first; rb < RB && ok; rb += rb_step) {
 #pragma unroll 1
-      for (int j = 0; j < J && ok; ++j) {
+      for (int jj = 0; jj < Js && ok; ++jj) {
+        const int j = j0 + jj;
         const int a = ucnt & 1;
         ok = warp_wait(ufull(a), (ucnt >> 1) & 1, 400 + a);
         if (!ok) break;
@@ -316,6 +334,26 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
       tc_fence_after();
       const int yc = part;
       const bool mine = yc < NY / 64 && yc * 64 < p.N;
+      if (S > 1) {
+        // Split row block (one per cluster): CTA s > 0 parks its partial in its operand ring
+        // for CTA 0, which combines and stores after the cluster barrier below.
+        if (srank > 0 && mine) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float v[32];
+            tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), v);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint32_t addr = sS + static_cast<uint32_t>((((ew * 2 + h) * 8 + q) * 32 + lane) * 16);
+              asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[4 * q]), "f"(v[4 * q + 1]),
+                           "f"(v[4 * q + 2]), "f"(v[4 * q + 3])
+                           : "memory");
+            }
+          }
+        }
+        ++rcnt;
+        break;
+      }
       if (mine) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -351,6 +389,57 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
     __syncwarp();
   }
 
+  if (S > 1) {
+    tc_fence_before();
+    cluster_sync();  // (1) every peer's Y partial is in its shared memory
+    tc_fence_after();
+    const int rb = rb_first;
+    const int ew = warp - kCtrlThreads / 32;
+    if (srank == 0 && warp >= kCtrlThreads / 32 && rb < RB && !*abort_flag) {
+      const int sub = warp & 3;
+      const int part = ew >> 2;
+      const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+      const uint32_t ystage = sH + static_cast<uint32_t>(ew * 4096);
+      const int yc = part;
+      if (yc < NY / 64 && yc * 64 < p.N) {
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          float v[32];
+          tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), v);
+#pragma unroll 1
+          for (int s2 = 1; s2 < S; ++s2) {  // rank order
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint32_t addr = sS + static_cast<uint32_t>((((ew * 2 + h) * 8 + q) * 32 + lane) * 16);
+              const float4 t = ld_cluster_f4(map_to_rank(addr, static_cast<uint32_t>(s2)));
+              v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
+            }
+          }
+          if (p.bias2) add_bias<BF16, 32>(v, p.bias2, yc * 64 + h * 32, p.N);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t addr = ystage + lane * 128 + (((h * 4 + c) ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
+                         "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+                         : "memory");
+          }
+        }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&p.tm_st_y, ystage, yc * 64, rb * kBM + sub * 32);
+          bulk_commit();
+          bulk_wait_all();
+        }
+        __syncwarp();
+      }
+    }
+    tc_fence_before();
+    cluster_sync();  // (2) no peer leaves before CTA 0 has read its partial
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

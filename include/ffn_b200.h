@@ -141,6 +141,8 @@ typedef struct {
   int64_t flag_words;       /* u32 Stream-K partial-ready flags: 2 x block_num */
   int64_t status_words;     /* i32 status words */
   int32_t schedule;         /* resolved schedule: 1 static, 2 dynamic */
+  int32_t row_split;        /* row-block plans: CTAs (one cluster) sharing each row block's H
+                               chunks, 1, 2 or 4; 1 for the other plans */
 } ffn_b200_plan;
 
 /* Device buffers.  ld* are row pitches in elements; each must be a multiple of 8 and each

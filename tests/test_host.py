@@ -98,9 +98,15 @@ def test_selection():
     # full_load_a: hidden row block on chip, Y row block in TMEM -> N <= 256 (BASELINE cfg2 yes, cfg1 no)
     cfg2 = problem_from_shapes([6993, 100], [1000, 100], [250, 1000])
     plan = make_plan(cfg2, Selection(down_impl="full_load_a"), sm_count=148)
-    assert plan.kernel["variant"] == 9 and plan.block_num == 55 and plan.kernel["tile_n"] == 256
+    # 55 row blocks on 148 SMs: clusters of 2 CTAs split each block's 8 H chunks
+    assert plan.kernel["variant"] == 9 and plan.block_num == 110 and plan.kernel["tile_n"] == 256
+    assert plan.kernel["row_split"] == 2
     assert plan.kernel["up"]["tiles_q"] == 8 and plan.kernel["up"]["k_blocks"] == 2
-    assert make_plan(cfg2, Selection(down_impl="full_load_a"), 16, sm_count=148).block_num == 16
+    small = make_plan(cfg2, Selection(down_impl="full_load_a"), 16, sm_count=148)
+    assert small.block_num == 16 and small.kernel["row_split"] == 1
+    many = make_plan(problem_from_shapes([512, 256], [1024, 256], [256, 1024]), Selection(down_impl="full_load_a"),
+                     sm_count=148)
+    assert many.kernel["row_split"] == 4 and many.block_num == 16
     with pytest.raises(NotApplicable):
         make_plan(problem_from_shapes([512, 512], [2048, 512], [512, 2048]), Selection(down_impl="full_load_a"),
                   sm_count=148)
