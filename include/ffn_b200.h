@@ -136,7 +136,8 @@ typedef struct {
   int64_t smem_bytes;
   ffn_b200_phase_plan up, down;
   int64_t workspace_floats; /* fp32 Stream-K partials: 2 phases x block_num x tile_m x tile_n */
-  int64_t counter_words;    /* u32 words: two u64 tile-claim counters (up, down), then the
+  int64_t counter_words;    /* u32 words: two u64 tile-claim counters (up, down), the u64
+                               launch count (the device-side launch epoch), then the
                                hidden-row-block readiness counters */
   int64_t flag_words;       /* u32 Stream-K partial-ready flags: 2 x block_num */
   int64_t status_words;     /* i32 status words */
