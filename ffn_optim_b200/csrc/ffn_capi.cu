@@ -79,9 +79,12 @@ KernelFn pick_kernel(int bf16, int act) {
 template <int NY>
 KernelFn pick_rowblock(int bf16, int act) {
   using namespace ffnb200;
-  if (bf16)
+  if (bf16) {
+    if (act == 3) return ffn_rowblock_kernel<NY, 4, true, 3>;
     return act == 2 ? ffn_rowblock_kernel<NY, 4, true, 2>
                     : (act == 1 ? ffn_rowblock_kernel<NY, 4, true, 1> : ffn_rowblock_kernel<NY, 4, true, 0>);
+  }
+  if (act == 3) return ffn_rowblock_kernel<NY, 4, false, 3>;
   return act == 2 ? ffn_rowblock_kernel<NY, 4, false, 2>
                   : (act == 1 ? ffn_rowblock_kernel<NY, 4, false, 1> : ffn_rowblock_kernel<NY, 4, false, 0>);
 }
@@ -182,7 +185,8 @@ int plan_rowblock(const ffn_b200_problem& pr, int grid, ffn_b200_plan* out) {
   }
   const Variant& v = kVariants[variant];
   const int64_t rows = cdiv(pr.m, ffnb200::kBM);
-  const int64_t chunks = cdiv(pr.h, 128);
+  // 128-row chunks of W1: H/128, or for SwiGLU's packed W1 (64 gate + 64 up rows) H/64.
+  const int64_t chunks = pr.gelu == FFN_B200_SWIGLU ? cdiv(pr.h, 64) : cdiv(pr.h, 128);
   if (rows * chunks >= (int64_t(1) << 31)) return FFN_B200_ERR_TOO_LARGE;
   // Few row blocks: clusters of S CTAs split each block's H chunks (S = 2 or 4 while S*rows
   // CTAs fit the grid and every CTA keeps at least one chunk); one row block per cluster.
@@ -347,7 +351,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
 
   std::memset(out, 0, sizeof(*out));
   if (pr->down_impl == FFN_B200_DOWN_FULL_LOAD_A) {
-    if (fp8w || pr->gelu == FFN_B200_SWIGLU) return FFN_B200_ERR_NOT_APPLICABLE;
+    if (fp8w) return FFN_B200_ERR_NOT_APPLICABLE;
     return plan_rowblock(*pr, grid, out);
   }
   if (pr->tile_variant > 0 && kVariants[pr->tile_variant - 1].rowblock) return FFN_B200_ERR_INVALID;
@@ -506,7 +510,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   if (rowblock) {
     // X [M,K] and W1 [H,K] in 128-row boxes, W2 [N,H] in one box of tile_n rows, Y stores.
     rc = encode_2d(&P.tm_a_up, b->x, dt, prob.k, prob.m, b->ldx, 64, 128);
-    if (!rc) rc = encode_2d(&P.tm_b_up, b->w1, dt, prob.k, prob.h, b->ldw1, 64, 128);
+    if (!rc) rc = encode_2d(&P.tm_b_up, b->w1, dt, prob.k, w1_rows, b->ldw1, 64, 128);
     if (!rc) rc = encode_2d(&P.tm_b_dn, b->w2, dt, prob.h, prob.n, b->ldw2, 64, static_cast<uint32_t>(plan.tile_n));
     if (!rc) rc = encode_2d(&P.tm_st_y, b->y, dt, prob.n, prob.m, b->ldy, 64, ffnb200::kStoreRows);
   } else if (!sw) {

@@ -59,6 +59,10 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
   constexpr uint32_t kIdescDn = make_idesc<BF16, NY, kBM>();
   constexpr uint32_t kUpBytes = 2 * kABytes;           // X k-block + W1 k-block (128 rows each)
   constexpr uint32_t kDnBytes = NY * kBK * 2;          // W2 k-block
+  // SwiGLU (GELU == 3): a 128-row chunk of the packed W1 holds 64 gate rows then the matching
+  // 64 up rows, so each chunk yields 64 hidden columns: one k-block of the down GEMM.
+  constexpr bool kGlu = GELU == 3;
+  constexpr int kHidKb = kGlu ? 1 : 2;                 // down k-blocks per chunk
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -166,10 +170,10 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
           }
           if (ok && jj >= 1) {  // down(j-1): the two W2 k-blocks of chunk j-1
 #pragma unroll 1
-            for (int kk = 0; kk < 2; ++kk) {
+            for (int kk = 0; kk < kHidKb; ++kk) {
               if (!next_stage()) { ok = false; break; }
               mbar_expect_tx(full_bar(stage), kDnBytes);
-              tma_load_2d(sS + stage * LY::kStage, &p.tm_b_dn, ((j - 1) * 2 + kk) * kBK, 0, full_bar(stage));
+              tma_load_2d(sS + stage * LY::kStage, &p.tm_b_dn, ((j - 1) * kHidKb + kk) * kBK, 0, full_bar(stage));
               advance();
             }
           }
@@ -225,7 +229,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         tc_fence_after();
         const uint32_t d = tmem_base + 256u;
 #pragma unroll 1
-        for (int kk = 0; kk < 2; ++kk) {
+        for (int kk = 0; kk < kHidKb; ++kk) {
           if (!wait_bar(full_bar(stage), phase, abort_flag, p, 300 + stage)) return false;
           tc_fence_after();
           const uint64_t da = sw128_desc(sH + b * LY::kHidBuf + kk * kABytes);
@@ -302,17 +306,28 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         if (!ok) break;
         tc_fence_after();
         float v[32];
-        tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(a * LY::kChunk + part * 32), v);
+        if constexpr (kGlu) {  // gate and up sums of hidden columns part*16 .. part*16+15
+          tmem_ld16(tmem_base + lane_off + static_cast<uint32_t>(a * LY::kChunk + part * 16), v);
+          tmem_ld16(tmem_base + lane_off + static_cast<uint32_t>(a * LY::kChunk + 64 + part * 16), v + 16);
+        } else {
+          tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(a * LY::kChunk + part * 32), v);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(uempty(a));
         ++ucnt;
-        if (p.bias1) add_bias<BF16, 32>(v, p.bias1, j * LY::kChunk + part * 32, p.H);
         uint32_t pk[16];
+        if constexpr (kGlu) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          gelu2<GELU>(v[2 * i], v[2 * i + 1]);
-          pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
+          for (int i = 0; i < 8; ++i)
+            pk[i] = pack2<BF16>(silu(v[2 * i]) * v[16 + 2 * i], silu(v[2 * i + 1]) * v[16 + 2 * i + 1]);
+        } else {
+          if (p.bias1) add_bias<BF16, 32>(v, p.bias1, j * LY::kChunk + part * 32, p.H);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            gelu2<GELU>(v[2 * i], v[2 * i + 1]);
+            pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
+          }
         }
         const int b = hcnt & 1;
         ok = warp_wait(hempty(b), ((hcnt >> 1) & 1) ^ 1u, 420 + b);
@@ -321,7 +336,18 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
           y_staged = false;
         }
         if (!ok) break;
-        store_quarter(hid_row(b), row, (part & 1) * 4, pk);
+        if constexpr (kGlu) {  // 16 columns = 16-byte chunks part*2, part*2+1 of k-block 0
+          const uint32_t row_addr = sH + static_cast<uint32_t>(b * LY::kHidBuf + row * 128);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t addr = row_addr + (((part * 2 + c) ^ (row & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
+                         "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+                         : "memory");
+          }
+        } else {
+          store_quarter(hid_row(b), row, (part & 1) * 4, pk);
+        }
         fence_async_shared();
         __syncwarp();
         if (lane == 0) mbar_arrive(hfull(b));

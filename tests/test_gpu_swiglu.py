@@ -6,8 +6,9 @@ each hidden value from its gate and up sums in fp32 before the one rounding of h
 tile family runs against the oracle of the same arithmetic within two output ulps plus
 1e-3 * max|ref|: one-CTA prefill tiles (four and eight epilogue warps), CTA pairs, Stream-K
 (the owner adds the gate and up partials), the swap-AB decode tiles with and without K-step
-chains, fp8-weight decode tiles; ragged H (a padded last 64-row block); full_load_a is not
-applicable (its hidden row block holds H columns of one GEMM).
+chains, fp8-weight decode tiles, hidden-resident row blocks (each 128-row chunk of the
+packed W1 gives 64 hidden columns, one down k-block; split over clusters for few row
+blocks); ragged H (a padded last 64-row block).
 """
 import numpy as np
 import pytest
@@ -49,8 +50,8 @@ def _unpack(z, h, swap_ab):
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s[:4])) + str(s[4])[-4:])
 @pytest.mark.parametrize("variant", [
     {}, {"down_impl": "streamk"}, {"tile": "cta128x128"}, {"tile": "pair256x256"}, {"tile": "swap16k4"},
-    {"tile": "swap64"}, {"weight_format": "fp8"}],
-    ids=["auto", "streamk", "epi8", "pair", "swap16k4", "swap64", "fp8"])
+    {"tile": "swap64"}, {"weight_format": "fp8"}, {"down_impl": "full_load_a"}],
+    ids=["auto", "streamk", "epi8", "pair", "swap16k4", "swap64", "fp8", "full_load_a"])
 def test_swiglu_vs_oracle(shape, variant):
     m, k, h, n, dtype = shape
     x, w1, w2, b2 = _inputs(m, k, h, n, dtype, m + 7 * h)
@@ -94,8 +95,9 @@ def test_swiglu_vs_oracle(shape, variant):
 
 def test_swiglu_rejections():
     x, w1, w2, _ = _inputs(256, 64, 128, 64, torch.bfloat16, 1)
-    with pytest.raises(NotApplicable):
-        prepare_ffn(x.cuda(), w1.cuda(), w2.cuda(), activation="swiglu", down_impl="full_load_a")
+    with pytest.raises(NotApplicable):  # full_load_a keeps Y in TMEM: N <= 256
+        prepare_ffn(x.cuda(), w1.cuda(), torch.zeros(300, 128, dtype=torch.bfloat16).cuda(), activation="swiglu",
+                    down_impl="full_load_a")
     with pytest.raises(ValueError):  # W1 must hold 2H rows
         prepare_ffn(x.cuda(), w1[:128].cuda(), w2.cuda(), activation="swiglu")
     with pytest.raises(ValueError):

@@ -312,7 +312,8 @@ def test_swiglu_packing_and_plan(lib):
         up = info.up.tiles_r if swap else info.up.tiles_q
         assert up == -(-rows // (128 if swap else info.tile_n))
     prob = _lib.Problem(16, 64, 520, 64, 1, 1, _lib.GELU_CODES["swiglu"], 0, 148)  # full_load_a
-    assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_NOT_APPLICABLE
+    assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.OK
+    assert info.up.tiles_q == 9 and info.swap_ab == 0  # 64 hidden columns per 128-row chunk
 
 
 def test_handle_setters_reject_null_and_bad_values(lib):
