@@ -24,10 +24,11 @@
 //
 // Few row blocks (M <= 128 * SMs / 2): a cluster of S = Params::rb_split CTAs shares each
 // row block, CTA s taking H chunks [s*J/S, (s+1)*J/S), so S times as many SMs work and
-// each walks 1/S of the chain.  At the end every CTA s > 0 leaves its fp32 Y partial in its
-// own (then idle) operand ring; after a cluster barrier CTA 0 reads them over distributed
-// shared memory and adds them to its accumulator in rank order (fixed, so the result is
-// the same on every run), and a second barrier keeps the peers resident until it has read.
+// each walks 1/S of the chain.  At the end every CTA leaves the fp32 Y partials of the
+// column chunks it does not finalise in its own (then idle) operand ring; Y column chunk yc is finalised by CTA yc % S, which after
+// a cluster barrier reads the other CTAs' partials of it over distributed shared memory and
+// sums all S in rank order (fixed, so the result is the same on every run); a second
+// barrier keeps every CTA resident until the others have read its partials.
 #pragma once
 
 #include "ffn_kernel.cuh"
@@ -361,9 +362,9 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
       const int yc = part;
       const bool mine = yc < NY / 64 && yc * 64 < p.N;
       if (S > 1) {
-        // Split row block (one per cluster): CTA s > 0 parks its partial in its operand ring
-        // for CTA 0, which combines and stores after the cluster barrier below.
-        if (srank > 0 && mine) {
+        // Split row block (one per cluster): Y chunk yc is finalised by CTA yc % S; the other
+        // CTAs park their partial of it in their operand ring, read after the cluster barrier.
+        if (mine && yc % S != srank) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float v[32];
@@ -411,7 +412,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
       y_staged = true;
       ++rcnt;
     }
-    if (lane == 0) bulk_wait_all();
+    if (lane == 0) bulk_wait_read0();  // staging read; the stores complete with the grid
     __syncwarp();
   }
 
@@ -421,25 +422,31 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
     tc_fence_after();
     const int rb = rb_first;
     const int ew = warp - kCtrlThreads / 32;
-    if (srank == 0 && warp >= kCtrlThreads / 32 && rb < RB && !*abort_flag) {
+    if (warp >= kCtrlThreads / 32 && rb < RB && !*abort_flag) {
       const int sub = warp & 3;
       const int part = ew >> 2;
       const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
       const uint32_t ystage = sH + static_cast<uint32_t>(ew * 4096);
       const int yc = part;
-      if (yc < NY / 64 && yc * 64 < p.N) {
+      if (yc < NY / 64 && yc * 64 < p.N && yc % S == srank) {  // the Y chunks this CTA finalises
 #pragma unroll 1
         for (int h = 0; h < 2; ++h) {
           float v[32];
-          tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), v);
 #pragma unroll 1
-          for (int s2 = 1; s2 < S; ++s2) {  // rank order
+          for (int s2 = 0; s2 < S; ++s2) {  // partials summed in rank order
+            float t[32];
+            if (s2 == srank) {
+              tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), t);
+            } else {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint32_t addr = sS + static_cast<uint32_t>((((ew * 2 + h) * 8 + q) * 32 + lane) * 16);
-              const float4 t = ld_cluster_f4(map_to_rank(addr, static_cast<uint32_t>(s2)));
-              v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
+              for (int q = 0; q < 8; ++q) {
+                const uint32_t addr = sS + static_cast<uint32_t>((((ew * 2 + h) * 8 + q) * 32 + lane) * 16);
+                const float4 f = ld_cluster_f4(map_to_rank(addr, static_cast<uint32_t>(s2)));
+                t[4 * q] = f.x; t[4 * q + 1] = f.y; t[4 * q + 2] = f.z; t[4 * q + 3] = f.w;
+              }
             }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = s2 == 0 ? t[i] : v[i] + t[i];
           }
           if (p.bias2) add_bias<BF16, 32>(v, p.bias2, yc * 64 + h * 32, p.N);
           uint32_t pk[16];
@@ -458,13 +465,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         if (lane == 0) {
           tma_store_2d(&p.tm_st_y, ystage, yc * 64, rb * kBM + sub * 32);
           bulk_commit();
-          bulk_wait_all();
+          bulk_wait_read0();
         }
         __syncwarp();
       }
     }
     tc_fence_before();
-    cluster_sync();  // (2) no peer leaves before CTA 0 has read its partial
+    cluster_sync();  // (2) no CTA leaves before the others have read its parked partials
   }
   tc_fence_before();
   __syncthreads();
