@@ -128,7 +128,7 @@ int tmem_cols_for(int variant) {
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 constexpr int kMinSplitKBlocks = 32;  // see make_plan: the up phase splits only tiles this long
-constexpr int kMinSegment = 8;        // minimum K steps of one CTA's Stream-K share
+constexpr int kMinSegment = 16;       // minimum K steps of one CTA's Stream-K share
 
 struct PhaseInput {
   int64_t rows, cols, depth;

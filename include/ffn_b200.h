@@ -123,7 +123,7 @@ typedef struct {
   int32_t tiles_r, tiles_q, tiles, k_blocks;
   int32_t dp_tiles, sk_tiles, sk_iters, sk_rem;
   int32_t group;
-  int32_t sk_ctas; /* CTAs sharing the Stream-K tail (the first sk_ctas; each gets >= 8 K steps) */
+  int32_t sk_ctas; /* CTAs sharing the Stream-K tail (the first sk_ctas; each gets >= 16 K steps) */
 } ffn_b200_phase_plan;
 
 typedef struct {
