@@ -22,7 +22,6 @@ ERR_CUDA = 5
 ERR_ALIGNMENT = 6
 ERR_TOO_LARGE = 7
 ERR_SCRATCH = 8
-ERR_EPOCH = 9
 NOALLOC_SCRATCH_BYTES = 32 << 20
 
 DTYPES = {"float16": 0, "bfloat16": 1}
@@ -33,6 +32,8 @@ TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pa
                  "swap16k4": 6, "swap64k2": 7, "rowblock64": 8, "rowblock128": 9, "rowblock256": 10,
                  "swap16fp8": 11, "swap64fp8": 12}
 WEIGHT_FORMATS = {"native": 0, "fp8": 1}
+# Element type of the partial tiles the fused reduce-scatter sends between GPUs.
+PARTIAL_TYPES = {"fp32": 0, "input": 1}
 L2_POLICIES = {"none": 1, "stream_b": 2, "normal": 3, "keep_a": 4}
 SCHEDULES = {"static": 1, "dynamic": 2}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",
@@ -145,8 +146,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             "ffn_b200_peer_open": ([vp, ctypes.POINTER(vp)], i32),
             "ffn_b200_peer_close": ([vp], i32),
             "ffn_b200_peer_free": ([vp], i32),
-            "ffn_b200_reduce_scatter_bytes": ([vp, i32, ctypes.POINTER(u64), ctypes.POINTER(u64)], i32),
-            "ffn_b200_set_reduce_scatter": ([vp, i32, i32, ctypes.POINTER(vp), ctypes.POINTER(vp), vp, i64], i32),
+            "ffn_b200_reduce_scatter_bytes": ([vp, i32, i32, ctypes.POINTER(u64), ctypes.POINTER(u64)], i32),
+            "ffn_b200_set_reduce_scatter": ([vp, i32, i32, i32, ctypes.POINTER(vp), ctypes.POINTER(vp), vp, i64], i32),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(lib, name)

@@ -22,11 +22,6 @@ class KernelCompilationError(RuntimeError):
     (reference ops/api.py:9-14 wraps DSL compile failures the same way)."""
 
 
-class EpochExhausted(RuntimeError):
-    """Kept for API compatibility: the launch epoch lives on the device and no longer runs
-    out, so ``run`` does not raise it."""
-
-
 @dataclass
 class PreparedFFN:
     """A prepared fused FFN that can be launched repeatedly (reference ops/api.py:17-45).
@@ -71,8 +66,6 @@ class PreparedFFN:
             if x is not None:
                 self.load_input(x)
             rc = _lib.load().ffn_b200_run(self.handle, ctypes.c_void_p(self.stream.cuda_stream))
-            if rc == _lib.ERR_EPOCH:
-                raise EpochExhausted(_lib.strerror(rc))
             if rc != _lib.OK:
                 raise RuntimeError(f"ffn_b200_run: {_lib.strerror(rc)}")
         return self._output_view()

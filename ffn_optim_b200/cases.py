@@ -119,20 +119,43 @@ def x_rows(case, start, stop):
     return out
 
 
+def _weight_bits(seed_seq, shape, dist, scale, dtype, chunk_rows=1024):
+    """One weight tensor from its own PCG64 stream, drawn in row chunks (the stream advances
+    exactly as in one call, so the values are the same) and rounded chunk by chunk."""
+    rng = np.random.Generator(np.random.PCG64(seed_seq))
+    out = np.empty(shape, dtype=np.uint16)
+    for r0 in range(0, shape[0], chunk_rows):
+        rows = min(chunk_rows, shape[0] - r0)
+        a = rng.standard_normal((rows, shape[1]), dtype=np.float32)
+        a *= np.float32(scale)
+        if dtype == "float16":
+            out[r0:r0 + rows] = a.astype(np.float16).view(np.uint16)
+        else:  # round to nearest even in place: u + 0x7FFF + ((u >> 16) & 1), then >> 16
+            u = a.view(np.uint32)
+            t = u >> np.uint32(16)
+            t &= np.uint32(1)
+            t += np.uint32(0x7FFF)
+            u += t
+            u >>= np.uint32(16)
+            out[r0:r0 + rows] = u
+    return out
+
+
 def weights(case):
-    """Bit patterns of W1 [H, K] and W2 [N, H]."""
+    """Bit patterns of W1 [H, K] and W2 [N, H] (drawn on two threads: independent streams)."""
+    from concurrent.futures import ThreadPoolExecutor
+
     p = case_problem(case)
     dist = case.get("distribution", "normal_fanin")
     _, s1, s2 = _streams(case)
-    r1 = np.random.Generator(np.random.PCG64(s1))
-    r2 = np.random.Generator(np.random.PCG64(s2))
     if dist == "normal_fanin":
-        w1 = r1.standard_normal((p.h, p.k), dtype=np.float32) * np.float32(p.k ** -0.5)
-        w2 = r2.standard_normal((p.n, p.h), dtype=np.float32) * np.float32(p.h ** -0.5)
+        scales = (p.k ** -0.5, p.h ** -0.5)
     else:
-        w1 = r1.standard_normal((p.h, p.k), dtype=np.float32) * np.float32(0.05)
-        w2 = r2.standard_normal((p.n, p.h), dtype=np.float32) * np.float32(0.05)
-    return _round_bits(w1, p.dtype), _round_bits(w2, p.dtype)
+        scales = (0.05, 0.05)
+    with ThreadPoolExecutor(2) as ex:
+        f1 = ex.submit(_weight_bits, s1, (p.h, p.k), dist, scales[0], p.dtype)
+        f2 = ex.submit(_weight_bits, s2, (p.n, p.h), dist, scales[1], p.dtype)
+        return f1.result(), f2.result()
 
 
 def make_arrays(case):
@@ -142,6 +165,28 @@ def make_arrays(case):
     x = x_rows(case, 0, rows_total).reshape(shape)
     w1, w2 = weights(case)
     return x, w1, w2
+
+
+def logical_x_rows(case, rows):
+    """Bit patterns [len(rows), K] of rows of the logical X (after the case's view and
+    stride), regenerating only the 4096-row blocks the rows fall in when X is plain."""
+    p = case_problem(case)
+    if case.get("x_view", "plain") == "transpose_last2" or case.get("noncontiguous", False):
+        import torch
+
+        x, _, _ = make_inputs(case)
+        flat = x.reshape(p.m, p.k).contiguous().view(torch.int16).numpy().view(np.uint16)
+        return flat[np.asarray(rows)]
+    blocks = {}
+    out = np.empty((len(rows), p.k), dtype=np.uint16)
+    for i, r in enumerate(rows):
+        b = int(r) // X_BLOCK_ROWS
+        if b not in blocks:
+            lo = b * X_BLOCK_ROWS
+            blocks[b] = (lo, x_rows(case, lo, min(lo + X_BLOCK_ROWS, p.m)))
+        lo, blk = blocks[b]
+        out[i] = blk[int(r) - lo]
+    return out
 
 
 def digest(*arrays):

@@ -258,6 +258,19 @@ int encode_2d(CUtensorMap* tm, const void* base, int dtype, int64_t inner, int64
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 2-D row-major fp32 tensor [outer, inner], pitch in elements; boxes of 32 x box_outer
+// (128-byte rows, 128B-swizzled): the fp32 staging of the fused reduce-scatter.
+int encode_2d_f32(CUtensorMap* tm, const void* base, int64_t inner, int64_t outer, int64_t pitch, uint32_t box_outer) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch) * 4};
+  cuuint32_t box[2] = {32, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FFN_B200_OK : FFN_B200_ERR_CUDA;
+}
+
 // 2-D row-major tensor of fp8 codes [outer, inner] (inner even), pitch in bytes, described to
 // the TMA as pairs of codes (16-bit elements: the copy engine's work follows the element
 // count, and the bytes and their swizzled placement are the same); box_inner in bytes; the
@@ -297,12 +310,11 @@ const char* ffn_b200_strerror(int code) {
     case FFN_B200_OK: return "ok";
     case FFN_B200_ERR_INVALID: return "invalid argument";
     case FFN_B200_ERR_NOT_APPLICABLE: return "Stream-K candidate has no remainder tiles or fewer than two K tiles";
-    case FFN_B200_ERR_UNAVAILABLE: return "implementation not available (full_load_a / full_load_b)";
+    case FFN_B200_ERR_UNAVAILABLE: return "implementation not available (full_load_b)";
     case FFN_B200_ERR_DEVICE: return "device is not sm_100 or block_num exceeds the SM count";
     case FFN_B200_ERR_CUDA: return "CUDA call failed";
     case FFN_B200_ERR_ALIGNMENT: return "buffer base not 16-byte aligned or pitch not a multiple of 8 elements";
     case FFN_B200_ERR_TOO_LARGE: return "problem does not fit one launch";
-    case FFN_B200_ERR_EPOCH: return "launch epoch exhausted (not returned: the epoch lives on the device)";
     case FFN_B200_ERR_SCRATCH:
       return "problem needs more scratch than the 32 MiB that ffn_b200_run_noalloc holds; use ffn_b200_prepare";
   }
@@ -763,21 +775,25 @@ int ffn_b200_peer_free(void* dev_ptr) {
   return FFN_B200_OK;
 }
 
-int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* h, int world, uint64_t* stage_bytes, uint64_t* flag_bytes) {
+int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* h, int world, int32_t partial, uint64_t* stage_bytes,
+                                  uint64_t* flag_bytes) {
   if (!h || !stage_bytes || !flag_bytes || world < 2 || world > ffnb200::kMaxRanks) return FFN_B200_ERR_INVALID;
+  if (partial != FFN_B200_PARTIAL_F32 && partial != FFN_B200_PARTIAL_INPUT) return FFN_B200_ERR_INVALID;
   const ffn_b200_plan& pl = h->plan;
   if (pl.swap_ab || pl.cta_pair || pl.down.tiles_r % world) return FFN_B200_ERR_INVALID;
   const uint64_t band = static_cast<uint64_t>(pl.down.tiles_r / world) * pl.down.tiles_q;
-  *stage_bytes = 2ull * world * band * ffnb200::kBM * pl.tile_n * 2;
+  const uint64_t esize = partial == FFN_B200_PARTIAL_F32 ? 4 : 2;
+  *stage_bytes = 2ull * world * band * ffnb200::kBM * pl.tile_n * esize;
   *flag_bytes = 4ull * world * band;
   return FFN_B200_OK;
 }
 
-int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, void* const* stage_ptrs,
+int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, int32_t partial, void* const* stage_ptrs,
                                 void* const* flag_ptrs, void* y_local, int64_t ldy_local) {
   if (!h || world < 2 || world > ffnb200::kMaxRanks || rank < 0 || rank >= world || !stage_ptrs || !flag_ptrs ||
       !y_local)
     return FFN_B200_ERR_INVALID;
+  if (partial != FFN_B200_PARTIAL_F32 && partial != FFN_B200_PARTIAL_INPUT) return FFN_B200_ERR_INVALID;
   const ffn_b200_plan& pl = h->plan;
   if (pl.swap_ab || pl.cta_pair || pl.down.tiles_r % world) return FFN_B200_ERR_INVALID;
   if (h->prob.m % (static_cast<int64_t>(world) * pl.tile_m) != 0) return FFN_B200_ERR_INVALID;
@@ -791,13 +807,16 @@ int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, void* c
   P.rs_world = world;
   P.rs_rank = rank;
   P.rs_band_tiles = pl.down.tiles_r / world;
+  P.rs_fp32 = partial == FFN_B200_PARTIAL_F32 ? 1 : 0;
   const int64_t stage_rows = 2ll * world * (pl.down.tiles_r / world) * pl.down.tiles_q * ffnb200::kBM;
   for (int r = 0; r < world; ++r) {
-    P.rs_stage[r] = static_cast<uint16_t*>(stage_ptrs[r]);
+    P.rs_stage[r] = stage_ptrs[r];
     P.rs_flags[r] = static_cast<unsigned*>(flag_ptrs[r]);
     // Bulk-store map over rank r's staging buffer ([rows][tile_n], no multicast).
-    const int e = encode_2d(&P.tm_rs[r], stage_ptrs[r], h->prob.dtype, pl.tile_n, stage_rows, pl.tile_n, 64,
-                            ffnb200::kStoreRows);
+    const int e = P.rs_fp32 ? encode_2d_f32(&P.tm_rs[r], stage_ptrs[r], pl.tile_n, stage_rows, pl.tile_n,
+                                            ffnb200::kStoreRows)
+                            : encode_2d(&P.tm_rs[r], stage_ptrs[r], h->prob.dtype, pl.tile_n, stage_rows, pl.tile_n,
+                                        64, ffnb200::kStoreRows);
     if (e) return e;
   }
   return FFN_B200_OK;

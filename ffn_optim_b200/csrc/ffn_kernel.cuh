@@ -97,11 +97,13 @@ struct Params {
   const uint16_t* bias2;       // the hidden sums before the activation / to Y before rounding
   // Fused reduce-scatter of the down phase across `rs_world` GPUs (tensor parallel over H):
   // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
-  // of another rank's band is pushed as a bf16 partial into that rank's staging buffer over
-  // NVLink; an owner sums the partials of its band in ascending rank order.
+  // of another rank's band is pushed as a partial (fp32, or rounded to the input dtype when
+  // rs_fp32 = 0) into that rank's staging buffer over NVLink; an owner sums the partials of
+  // its band in ascending rank order.
   int rb_split;          // row-block kernel: CTAs (a cluster) sharing one row block's H chunks
   int rs_world, rs_rank, rs_band_tiles;
-  uint16_t* rs_stage[kMaxRanks];   // per rank: [2 parity][world][band tiles][kBM][BN] bf16
+  int rs_fp32;                     // 1: staged partials are fp32; 0: the input dtype
+  void* rs_stage[kMaxRanks];       // per rank: [2 parity][world][band tiles][kBM][BN] partials
   unsigned* rs_flags[kMaxRanks];   // per rank: [world][band tiles] push counts (4 per launch)
   CUtensorMap tm_rs[kMaxRanks];    // store maps over each rank's staging, viewed as [rows][BN]
 };
@@ -1504,10 +1506,10 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
           }
         }
       }
-      auto rs_slot = [&](int dst_rank, int src) {  // this thread's row of a staging slot
+      auto rs_row = [&](int src) {  // element offset of this thread's row in a staging slot
         const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
         const size_t slot = ((static_cast<size_t>(epoch & 1u) * p.rs_world + src) * band + rs_tile) * kBM + row;
-        return p.rs_stage[dst_rank] + slot * BN;
+        return slot * BN;
       };
 
       if constexpr (!SWAP) {
@@ -1580,8 +1582,22 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
                 if (src == p.rs_rank) {
 #pragma unroll
                   for (int j = 0; j < 16; ++j) acc[j] = src == 0 ? v[16 * q + j] : acc[j] + v[16 * q + j];
+                } else if (p.rs_fp32) {
+                  const float4* sp = reinterpret_cast<const float4*>(static_cast<const float*>(p.rs_stage[p.rs_rank]) +
+                                                                     rs_row(src) + ch * 64 + 16 * q);
+                  float4 w[4];
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) w[j] = __ldcg(sp + j);
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    acc[4 * j] = src == 0 ? w[j].x : acc[4 * j] + w[j].x;
+                    acc[4 * j + 1] = src == 0 ? w[j].y : acc[4 * j + 1] + w[j].y;
+                    acc[4 * j + 2] = src == 0 ? w[j].z : acc[4 * j + 2] + w[j].z;
+                    acc[4 * j + 3] = src == 0 ? w[j].w : acc[4 * j + 3] + w[j].w;
+                  }
                 } else {
-                  const uint4* sp = reinterpret_cast<const uint4*>(rs_slot(p.rs_rank, src) + ch * 64 + 16 * q);
+                  const uint4* sp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.rs_stage[p.rs_rank]) +
+                                                                   rs_row(src) + ch * 64 + 16 * q);
 #pragma unroll
                   for (int j = 0; j < 2; ++j) {
                     const uint4 w = __ldcg(sp + j);
@@ -1600,6 +1616,35 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             }
             // (the band owner adds the bias once, to the sum of all ranks' partials)
             if (p.bias2) add_bias<BF16, 64>(v, p.bias2, tq * BN + ch * 64, p.N);
+          }
+          if (rs_push && p.rs_fp32) {
+            // fp32 partial for the owning GPU: two 32-column halves (128-byte rows), each
+            // staged 128B-swizzled in one of this warp's buffers and sent as one 4 KB bulk
+            // store over NVLink, so the owner's sum sees the unrounded partial.
+            const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
+            const int srow = static_cast<int>(((static_cast<size_t>(epoch & 1u) * p.rs_world + p.rs_rank) * band +
+                                               rs_tile) * kBM) + sub * 32;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const uint32_t sb = sE + static_cast<uint32_t>((ew * 2 + sbuf) * kStageBufBytes);
+              if (lane == 0) bulk_wait_read1();
+              __syncwarp();
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t addr = sb + lane * 128 + ((j ^ (lane & 7)) << 4);
+                asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[32 * hh + 4 * j]),
+                             "f"(v[32 * hh + 4 * j + 1]), "f"(v[32 * hh + 4 * j + 2]), "f"(v[32 * hh + 4 * j + 3])
+                             : "memory");
+              }
+              fence_async_shared();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&p.tm_rs[rs_owner], sb, ch * 64 + 32 * hh, srow);
+                bulk_commit();
+              }
+              sbuf ^= 1;
+            }
+            continue;
           }
           uint32_t pk[32];
 #pragma unroll

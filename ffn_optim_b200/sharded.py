@@ -198,6 +198,12 @@ class RowShardedFFN:
     def run(self):
         return self.prepared.run()
 
+    def run_host(self, x_host, y_host, chunks=8):
+        """This rank's rows from host memory to host memory (``PreparedFFN.run_host``):
+        ``x_host`` [rows, K] and ``y_host`` [rows, N] are pinned CPU tensors of this rank's
+        ``m_slices`` rows; copies overlap the kernels of other row chunks."""
+        return self.prepared.run_host(x_host, y_host, chunks=chunks)
+
     def check(self):
         self.prepared.check()
 
@@ -212,16 +218,22 @@ class FusedTensorParallelFFN:
     """H-sharded fused FFN whose reduce-scatter runs inside the kernel, over NVLink.
 
     Same partitioning as :class:`TensorParallelFFN` (rank r holds W1 rows / W2 columns of
-    ``h_slice(H, r, P)``), but no NCCL call: during the down phase each rank pushes the bf16
+    ``h_slice(H, r, P)``), but no NCCL call: during the down phase each rank pushes the
     partial of every tile outside its own M/P-row band straight into the owning rank's
-    staging buffer (peer stores, then a system-scope release), and each rank sums the P
-    partials of its own band in ascending rank order and stores its Y rows.  Staging and
+    staging buffer (peer bulk stores, then a system-scope release), and each rank sums the P
+    partials of its own band in ascending rank order and stores its Y rows.  ``partial``
+    selects what crosses NVLink: ``'fp32'`` (default; the owner sums unrounded partials, so
+    every output keeps the single-GPU error bound) or ``'input'`` (partials rounded to the
+    input dtype: half the NVLink bytes, up to P-1 extra roundings per output).  Staging and
     push-count buffers are CUDA IPC buffers exchanged once at construction.  :meth:`run`
     launches one kernel and returns this rank's rows ``local_rows()`` of Y.
+
+    :meth:`close` is collective: every rank calls it together (it synchronises and meets the
+    other ranks before releasing memory that their kernels write into).
     """
 
     def __init__(self, x, w1, w2, *, group=None, sliced=False, down_impl="basic", block_num=None,
-                 gelu="rational", tile="cta128x256"):
+                 gelu="rational", tile="cta128x256", partial="fp32"):
         import torch
         import torch.distributed as dist
 
@@ -229,9 +241,13 @@ class FusedTensorParallelFFN:
         from .api import prepare_ffn
         from .host.inputs import pitch_of
 
+        if partial not in _lib.PARTIAL_TYPES:
+            raise ValueError(f"partial must be one of {sorted(_lib.PARTIAL_TYPES)}")
+        self.partial = partial
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self._own, self._opened, self._closed = [], [], False
         k = x.shape[-1]
         m = x.numel() // k
         if not sliced:
@@ -243,10 +259,10 @@ class FusedTensorParallelFFN:
                                     tile=tile)
         lib = _lib.load()
         h = self.prepared.handle
+        code = _lib.PARTIAL_TYPES[partial]
         sb, fb = ctypes.c_uint64(), ctypes.c_uint64()
-        if lib.ffn_b200_reduce_scatter_bytes(h, self.world, ctypes.byref(sb), ctypes.byref(fb)) != _lib.OK:
+        if lib.ffn_b200_reduce_scatter_bytes(h, self.world, code, ctypes.byref(sb), ctypes.byref(fb)) != _lib.OK:
             raise ValueError("fused reduce-scatter needs M divisible by world*tile rows and a one-CTA prefill tile")
-        self._own = []
         handles = []
         with torch.cuda.device(x.device):
             for size in (sb.value, fb.value):
@@ -258,7 +274,6 @@ class FusedTensorParallelFFN:
                 handles.append(bytes(ipc))
             everyone = [None] * self.world
             dist.all_gather_object(everyone, handles, group=group)
-            self._opened = []
             stage = (ctypes.c_void_p * self.world)()
             flags = (ctypes.c_void_p * self.world)()
             for r in range(self.world):
@@ -275,7 +290,7 @@ class FusedTensorParallelFFN:
                     ptrs.append(ptr)
                 stage[r], flags[r] = ptrs
             self.y = torch.empty((m // self.world, pitch_of(self.n)), dtype=x.dtype, device=x.device)
-            rc = lib.ffn_b200_set_reduce_scatter(h, self.world, self.rank, stage, flags, self.y.data_ptr(),
+            rc = lib.ffn_b200_set_reduce_scatter(h, self.world, self.rank, code, stage, flags, self.y.data_ptr(),
                                                  self.y.stride(0))
             if rc != _lib.OK:
                 raise ValueError(f"ffn_b200_set_reduce_scatter: {_lib.strerror(rc)}")
@@ -286,13 +301,9 @@ class FusedTensorParallelFFN:
         return 1
 
     def run(self):
-        from .api import EpochExhausted
-
-        try:
-            self.prepared.run()
-        except EpochExhausted:
-            self.collective_reset()
-            self.prepared.run()
+        if self._closed:
+            raise RuntimeError("FusedTensorParallelFFN has been closed")
+        self.prepared.run()
         return self.y[:, :self.n]
 
     def collective_reset(self):
@@ -315,17 +326,35 @@ class FusedTensorParallelFFN:
         self.prepared.check()
 
     def close(self):
+        """Releases the peer mappings and this rank's staging buffers.  Collective: every rank
+        calls it at the same point.  This rank's kernels are complete (synchronize) and every
+        other rank's are too (barrier) before any buffer a peer kernel writes into is freed,
+        so no GPU ever stores into freed memory, even after a launch that timed out."""
+        import torch
+        import torch.distributed as dist
+
         from . import _lib
 
-        lib = _lib.load()
-        for ptr in getattr(self, "_opened", []):
+        if self._closed:
+            return
+        with torch.cuda.device(self.y.device):
+            torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self._release(_lib.load())
+
+    def _release(self, lib):
+        for ptr in self._opened:
             lib.ffn_b200_peer_close(ptr)
-        for ptr in getattr(self, "_own", []):
+        for ptr in self._own:
             lib.ffn_b200_peer_free(ptr)
-        self._opened, self._own = [], []
+        self._opened, self._own, self._closed = [], [], True
 
     def __del__(self):
-        try:
-            self.close()
-        except Exception:  # noqa: BLE001 - interpreter shutdown
-            pass
+        # Without the collective close() no rank can know that the other GPUs have stopped
+        # writing into this rank's staging buffers, so they are left allocated (leaked until
+        # the process exits) rather than freed under a peer's stores.
+        if not getattr(self, "_closed", True) and getattr(self, "_own", None):
+            import warnings
+
+            warnings.warn("FusedTensorParallelFFN dropped without close(): peer-visible buffers are leaked",
+                          ResourceWarning, stacklevel=2)

@@ -4,8 +4,12 @@
  *     Y = GELU(X . W1^T) . W2^T      (fp16 or bf16, no bias, inference only)
  *
  * X is [M, K] row-major, W1 is [H, K] (torch Linear layout), W2 is [N, H], Y is [M, N].
- * All pointers are device pointers owned by the caller; the library allocates no device
- * memory and never synchronises the stream it is given.
+ * All pointers are device pointers owned by the caller, and no entry point synchronises the
+ * stream it is given.  The one entry point that allocates device memory is
+ * ffn_b200_peer_alloc (cudaMalloc of a peer-visible buffer for the multi-GPU path).  The
+ * library also holds static device arrays on every GPU that loads it, until the process
+ * exits: the 32 MiB scratch of ffn_b200_run_noalloc (FFN_B200_NOALLOC_SCRATCH_BYTES) and
+ * 10 KiB for the CTA-pair placement map and its probe (int32[512] + int32[2][1024]).
  *
  * Each entry point replaces one piece of the reference implementation (hxtsg/ffn_optim):
  *
@@ -30,7 +34,7 @@
 extern "C" {
 #endif
 
-#define FFN_B200_ABI_VERSION 1
+#define FFN_B200_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define FFN_B200_EXPORT __attribute__((visibility("default")))
@@ -42,13 +46,12 @@ typedef enum {
   FFN_B200_OK = 0,
   FFN_B200_ERR_INVALID = 1,        /* bad shape, pointer, pitch or enum (reference: ValueError) */
   FFN_B200_ERR_NOT_APPLICABLE = 2, /* streamk without a tail wave (reference: NotApplicable) */
-  FFN_B200_ERR_UNAVAILABLE = 3,    /* full_load_a / full_load_b (reference: DependencyUnavailable) */
+  FFN_B200_ERR_UNAVAILABLE = 3,    /* full_load_b (reference: DependencyUnavailable) */
   FFN_B200_ERR_DEVICE = 4,         /* not an sm_100 device or block_num > SM count */
   FFN_B200_ERR_CUDA = 5,           /* a CUDA runtime / driver call failed */
   FFN_B200_ERR_ALIGNMENT = 6,      /* base not 16-byte aligned or pitch not a multiple of 8 elements */
   FFN_B200_ERR_TOO_LARGE = 7,      /* tile count does not fit one launch */
-  FFN_B200_ERR_SCRATCH = 8,        /* needs more scratch than ffn_b200_run_noalloc holds */
-  FFN_B200_ERR_EPOCH = 9           /* kept for ABI stability; no longer returned (the launch epoch lives on the device) */
+  FFN_B200_ERR_SCRATCH = 8         /* needs more scratch than ffn_b200_run_noalloc holds */
 } ffn_b200_status;
 
 typedef enum { FFN_B200_F16 = 0, FFN_B200_BF16 = 1 } ffn_b200_dtype;
@@ -61,11 +64,9 @@ typedef enum {
   FFN_B200_DOWN_STREAMK = 3
 } ffn_b200_down_impl;
 
-/* GELU form used in the up-projection epilogue.  RATIONAL is the reference kernel's
- * clipped rational erf (ops/kernel/ffn.py:548-572, validation/reference.py:5-13);
- * ERF calls CUDA's erff. */
 /* Activation of the hidden layer (the problem's `gelu` field): the reference kernel's rational
- * GELU, the exact-erf GELU, SiLU (z * sigmoid(z)), or SwiGLU (SiLU(x.Wg^T) * (x.Wu^T)); the
+ * GELU (its clipped rational erf, ops/kernel/ffn.py:548-572, validation/reference.py:5-13),
+ * the exact-erf GELU (CUDA's erff), SiLU (z * sigmoid(z)), or SwiGLU (SiLU(x.Wg^T) * (x.Wu^T)); the
  * last two are beyond the reference's V1.  For SwiGLU, h is the hidden width and W1 holds
  * ffn_b200_swiglu_rows(h, plan.swap_ab) rows: with swap_ab == 0, blocks of 64 gate rows each
  * followed by the matching 64 up rows (zero rows pad the last block); with swap_ab == 1, gate
@@ -101,7 +102,10 @@ typedef struct {
   /* Tuning overrides, 0 = automatic (benchmarks and tests use them): */
   int32_t tile_variant; /* 1 + variant id forces one kernel variant
                            (1: 128x256, 2: 128x128, 3: swap 16, 4: swap 64, 5: CTA pair 256x256,
-                            6: swap 16 with 256-wide K stages, 7: swap 64 with 128-wide K stages) */
+                            6: swap 16 with 256-wide K stages, 7: swap 64 with 128-wide K stages,
+                            8/9/10: hidden-resident row blocks with a 64/128/256-column Y
+                            (down_impl full_load_a only), 11/12: swap 16 / swap 64 with fp8
+                            weights (weight_format FFN_B200_WEIGHTS_FP8_ROWS only)) */
   int32_t raster_group; /* tile rows per raster group (default: balances A and B bytes per wave) */
   int32_t l2_policy;    /* 1: no L2 eviction hints (default); 2: evict-last on the row operand and
                            evict-first on the column operand (measured: far more DRAM traffic);
@@ -216,20 +220,27 @@ FFN_B200_EXPORT int ffn_b200_peer_open(const void* ipc_handle, void** dev_ptr);
 FFN_B200_EXPORT int ffn_b200_peer_close(void* dev_ptr);
 FFN_B200_EXPORT int ffn_b200_peer_free(void* dev_ptr);
 
-/* Sizes of one rank's staging buffer (bf16 partial tiles, two launch parities) and push
- * counts for a `world`-GPU reduce-scatter of this handle's down phase. */
-FFN_B200_EXPORT int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* handle, int world, uint64_t* stage_bytes,
-                                                  uint64_t* flag_bytes);
+/* Element type of the partial Y tiles that the fused reduce-scatter sends between GPUs:
+ * fp32 (default: the owner sums unrounded partials, so P GPUs keep the single-GPU error
+ * bound) or the input dtype (half the NVLink bytes; each partial is rounded once before the
+ * sum, which adds up to P-1 roundings to every output). */
+typedef enum { FFN_B200_PARTIAL_F32 = 0, FFN_B200_PARTIAL_INPUT = 1 } ffn_b200_partial;
+
+/* Sizes of one rank's staging buffer (partial tiles of type `partial`, two launch
+ * parities) and push counts for a `world`-GPU reduce-scatter of this handle's down phase. */
+FFN_B200_EXPORT int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* handle, int world, int32_t partial,
+                                                  uint64_t* stage_bytes, uint64_t* flag_bytes);
 
 /* Turns the handle's down phase into a fused reduce-scatter over `world` GPUs: this rank
  * (`rank`) owns Y rows [rank*M/world, (rank+1)*M/world), written to `y_local`
  * ([M/world, ldy_local]); stage_ptrs[r] / flag_ptrs[r] are rank r's staging and count
  * buffers as mapped in this process (own ones included).  Every rank runs its handle once
- * per step; partial tiles of other bands are pushed over NVLink during the epilogue and
- * summed by their owner in ascending rank order.  Needs M divisible by world*128 and a
+ * per step; partial tiles of other bands (of type `partial`, the same on every rank) are
+ * pushed over NVLink during the epilogue and summed by their owner in ascending rank order.  Needs M divisible by world*128 and a
  * one-CTA prefill tile.  After a kernel error all ranks reset together. */
-FFN_B200_EXPORT int ffn_b200_set_reduce_scatter(ffn_b200_handle* handle, int world, int rank, void* const* stage_ptrs,
-                                                void* const* flag_ptrs, void* y_local, int64_t ldy_local);
+FFN_B200_EXPORT int ffn_b200_set_reduce_scatter(ffn_b200_handle* handle, int world, int rank, int32_t partial,
+                                                void* const* stage_ptrs, void* const* flag_ptrs, void* y_local,
+                                                int64_t ldy_local);
 
 /* Overlapped launches (programmatic dependent launch; off by default): with enable = 1,
  * each later run lets its CTAs start, and set up their barriers and tensor memory, while

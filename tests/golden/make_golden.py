@@ -56,23 +56,7 @@ def pick_rows(case, m):
 
 def logical_x_rows(case, rows):
     """Bit patterns [len(rows), K] of the logical X rows (handles the transposed view)."""
-    p = C.case_problem(case)
-    if case.get("x_view", "plain") == "transpose_last2" or case.get("noncontiguous", False):
-        x, _, _ = C.make_inputs(case)
-        import torch
-
-        flat = x.reshape(p.m, p.k).contiguous().view(torch.int16).numpy().view(np.uint16)
-        return flat[rows]
-    blocks = {}
-    out = np.empty((len(rows), p.k), dtype=np.uint16)
-    for i, r in enumerate(rows):
-        b = int(r) // C.X_BLOCK_ROWS
-        if b not in blocks:
-            lo = b * C.X_BLOCK_ROWS
-            blocks[b] = (lo, C.x_rows(case, lo, min(lo + C.X_BLOCK_ROWS, p.m)))
-        lo, blk = blocks[b]
-        out[i] = blk[int(r) - lo]
-    return out
+    return C.logical_x_rows(case, rows)
 
 
 def main():

@@ -1,6 +1,17 @@
-"""Multi-GPU paths on 2 GPUs (skipped with fewer): H-sharded with NCCL reduce-scatter,
-H-sharded with the reduce-scatter fused into the kernel (NVLink peer stores), and M-sharded,
-each against the single-GPU fused FFN on the same inputs."""
+"""Multi-GPU paths against the CPU oracle (skipped with fewer than 2 GPUs).
+
+At world size 2 and at every GPU of the box (``torch.cuda.device_count()``), one process per
+GPU over NCCL: H-sharded tensor parallelism with the reduce-scatter fused into the kernel
+(fp32 partials, the default, and input-dtype partials), H-sharded with an NCCL
+reduce-scatter, and M-sharded.  Every rank's output rows are checked against the oracle
+(``oracle/ffn_oracle.py``, the numpy restatement of the reference's ``ffn_torch``) on the
+same inputs: the reference criterion with the max-abs bound (``compare(strict=True)``)
+against the exact-erf golden for every variant, and the single-GPU bound -- two output ulps
++ 1e-3*max|golden| against the golden of the kernel's arithmetic (rational GELU, staged
+hidden) -- for the variants that sum unrounded partials (fp32 reduce-scatter, M-shard).
+The variants that round each rank's partial to bf16 before the cross-GPU sum get a floor of
+4e-3*max|golden| instead (up to P-1 extra roundings).
+"""
 import os
 import socket
 
@@ -11,7 +22,7 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-SHAPE = (1024, 512, 1024, 384)  # M, K, H, N
+SHAPE = (4096, 1024, 4096, 1024)  # M, K, H, N: M divisible by 8 ranks x 128-row tiles
 
 
 def _free_port():
@@ -34,7 +45,6 @@ def _worker(rank, world, port, out_dir):
 
     import torch.distributed as dist
 
-    from ffn_optim_b200 import prepare_ffn
     from ffn_optim_b200.sharded import FusedTensorParallelFFN, RowShardedFFN, TensorParallelFFN
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -43,41 +53,73 @@ def _worker(rank, world, port, out_dir):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
         x, w1, w2 = (t.to(dev) for t in _inputs())
-        full = prepare_ffn(x, w1, w2).run().float().cpu().numpy()
+        out = {}
         tp = TensorParallelFFN(x, w1, w2, chunks=2)
-        y_tp = tp.run().float().cpu().numpy()
+        out["nccl"] = tp.run().float().cpu().numpy()
         tp.check()
-        fused = FusedTensorParallelFFN(x, w1, w2)
-        for _ in range(3):  # repeated launches exercise both staging parities
-            y_f = fused.run()
-        fused.check()
-        y_f = y_f.float().cpu().numpy()
+        out["nccl_rows"] = np.array(tp.local_rows())
+        for partial in ("fp32", "input"):
+            fused = FusedTensorParallelFFN(x, w1, w2, partial=partial)
+            first = None
+            for i in range(3):  # repeated launches exercise both staging parities
+                y = fused.run()
+                fused.check()
+                if i == 0:
+                    first = y.clone()
+            out[f"fused_{partial}"] = y.float().cpu().numpy()
+            out[f"fused_{partial}_rows"] = np.array(fused.local_rows())
+            out[f"fused_{partial}_repeat_equal"] = np.array(bool(torch.equal(first, y)))
+            fused.close()
         ms = RowShardedFFN(x, w1, w2)
-        y_m = ms.run().float().cpu().numpy()
-        np.savez(os.path.join(out_dir, f"r{rank}.npz"), full=full, tp=y_tp, tp_rows=np.array(tp.local_rows()),
-                 fused=y_f, fused_rows=np.array(fused.local_rows()), m=y_m, m_lo=ms.lo, m_hi=ms.hi)
-        fused.close()
+        out["m"] = ms.run().float().cpu().numpy()
+        ms.check()
+        out["m_rows"] = np.arange(ms.lo, ms.hi)
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), **out)
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def _close(what, got, want, floor=4e-3):
-    # 2 output ulps + floor * max|want|; the H-sharded variants round their partials to bf16
-    # before the cross-GPU sum, the M-sharded one differs only by its Stream-K split
-    bound = 2.0 ** -6 * np.abs(want) + floor * np.abs(want).max()
-    assert np.all(np.abs(got - want) <= bound), (what, float(np.max(np.abs(got - want) - bound)))
+def _oracle():
+    from oracle import ffn_oracle as O
+
+    x, w1, w2 = (t.float().numpy() for t in _inputs())
+    staged = O.from_bits(O.ffn(x, w1, w2, "bfloat16", staged=True, rational=True), "bfloat16")
+    golden = O.from_bits(O.ffn(x, w1, w2, "bfloat16"), "bfloat16")
+    return staged, golden
+
+
+def _check(what, got, staged, golden, floor):
+    from ffn_optim_b200 import compare
+
+    r = compare(torch.from_numpy(got), torch.from_numpy(golden), strict=True)
+    assert r["passed"], (what, r)
+    bound = 2.0 ** -6 * np.abs(staged) + floor * np.abs(staged).max()
+    excess = np.abs(got - staged) - bound
+    assert np.all(excess <= 0), (what, float(excess.max()))
+
+
+def _worlds():
+    n = torch.cuda.device_count()
+    return sorted({2, min(n, 8)}) if n >= 2 else [2]
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_variants_match_single_gpu(tmp_path):
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
-    for r in range(2):
+@pytest.mark.parametrize("world", _worlds())
+def test_sharded_variants_vs_oracle(tmp_path, world):
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    staged, golden = _oracle()
+    seen = {k: np.zeros(SHAPE[0], dtype=bool) for k in ("nccl", "fused_fp32", "fused_input", "m")}
+    for r in range(world):
         d = np.load(tmp_path / f"r{r}.npz")
-        full = d["full"]
-        _close("nccl", d["tp"], full[d["tp_rows"]])
-        _close("fused", d["fused"], full[d["fused_rows"]])
-        _close("m-shard", d["m"], full[int(d["m_lo"]):int(d["m_hi"])], floor=1e-3)
+        for key, floor in (("fused_fp32", 1e-3), ("m", 1e-3), ("fused_input", 4e-3), ("nccl", 4e-3)):
+            rows = d[f"{key}_rows"]
+            _check(f"{key} rank {r} of {world}", d[key], staged[rows], golden[rows], floor)
+            seen[key][rows] = True
+        for partial in ("fp32", "input"):
+            assert bool(d[f"fused_{partial}_repeat_equal"]), f"fused {partial}: run-to-run results differ"
+    for key, mask in seen.items():
+        assert mask.all(), f"{key}: rows not covered by any rank"
 
 
 def _dead_rank_worker(rank, world, port, out_dir):

@@ -246,7 +246,7 @@ def test_library_exports_every_declared_symbol(lib):
     assert set(names) == set(_lib.EXPORTED)
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.ffn_b200_abi_version() == 1
+    assert lib.ffn_b200_abi_version() == 2
     assert lib.ffn_b200_strerror(2).decode().startswith("Stream-K")
 
 

@@ -9,8 +9,11 @@ its own, and the caller only passes X, W1, W2 and Y.
 
 This test calls that entry point through the C ABI twice in a row and checks each output
 against the regular prepared entry point (ffn_b200_prepare / ffn_b200_run) on the same
-inputs, with the tolerance of the other GPU parity tests.  It lives in its own file,
-collected last, and depends on no state left by other tests.
+inputs, with the tolerance of the other GPU parity tests, and against the CPU oracle (the
+numpy restatement of the reference's ffn_torch): two output ulps + 1e-3*max|golden| against
+the golden of the kernel's arithmetic, and the reference criterion with the max-abs bound
+against the exact-erf golden.  It lives in its own file, collected last, and depends on no
+state left by other tests.
 """
 import ctypes
 
@@ -19,7 +22,8 @@ import torch
 
 from ffn_optim_b200 import _lib, prepare_ffn
 from ffn_optim_b200.host.inputs import pitch_of
-from tests.test_gpu_parity import assert_close_bits, bits_of
+from oracle import ffn_oracle as O
+from tests.test_gpu_parity import assert_close_bits, assert_criterion, bits_of
 
 pytestmark = pytest.mark.gpu
 
@@ -58,6 +62,9 @@ def test_noalloc_matches_prepared_entry_point(shape):
     expected = prepared.run().clone()
     prepared.check()
     dt = str(dtype).removeprefix("torch.")
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    staged = O.ffn(f(x), f(w1), f(w2), dt, staged=True, rational=True)
+    golden = O.ffn(f(x), f(w1), f(w2), dt)
     prob = _lib.Problem(m, k, h, n, _lib.DTYPES[dt], _lib.DOWN_IMPL_CODES[down], 0, 0, 0)
     y = torch.full((m, pitch_of(n)), float("nan"), dtype=dtype, device="cuda")
     status = torch.full((4,), -1, dtype=torch.int32, device="cuda")
@@ -66,7 +73,10 @@ def test_noalloc_matches_prepared_entry_point(shape):
         assert rc == _lib.OK, _lib.strerror(rc)
         torch.cuda.synchronize()
         assert status.tolist()[0] == 0, (call, status.tolist())
-        assert_close_bits(bits_of(y[:, :n]), bits_of(expected), dt)
+        got = bits_of(y[:, :n])
+        assert_close_bits(got, bits_of(expected), dt)
+        assert_close_bits(got, staged, dt)
+        assert_criterion(got, golden, dt)
         y.fill_(float("nan"))
 
 
