@@ -82,6 +82,9 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-per-config", action="store_true")
     ap.add_argument("--no-variants", action="store_true", help="N>1: time only the --shard variant")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="override M (the workload's K, H, N and weights; X drawn on the device; no golden "
+                         "fixture, so no parity key): e.g. --workload cfg3_bf16 --rows 64 runs the swap64 decode tiles")
     return ap.parse_args()
 
 
@@ -202,7 +205,7 @@ def _tensor(bits, dtype, device):
     return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(dtype).to(device)
 
 
-def case_inputs(case, device, world=1, rank=0):
+def case_inputs(case, device, world=1, rank=0, rows=None):
     """The case's seeded inputs on `device` and its golden fixture.
 
     Weights: the case's PCG64 streams (rank 0 draws them and broadcasts when world > 1).
@@ -214,16 +217,19 @@ def case_inputs(case, device, world=1, rank=0):
 
     from ffn_optim_b200 import cases as C
 
+    if rows is not None:  # the workload's weights with `rows` tokens; no fixture for this shape
+        case = dict(case, shape=[rows, case["shape"][-1]], x_view="plain", noncontiguous=False)
     p = C.case_problem(case)
     dt = getattr(torch, p.dtype)
-    fx = dict(np.load(GOLDEN / f"{case['case_id']}.npz"))
-    if p.m <= 8192:
+    fx = None if rows is not None else dict(np.load(GOLDEN / f"{case['case_id']}.npz"))
+    if p.m <= 8192 and fx is not None:
         x, w1, w2 = C.make_inputs(case, device=device)
         return p, x, w1, w2, fx
     g = torch.Generator(device=device).manual_seed(7)
     x = torch.randn((p.m, p.k), generator=g, device=device, dtype=torch.float32).to(dt)
-    rows = torch.as_tensor(fx["rows"], device=device)
-    x[rows] = _tensor(C.logical_x_rows(case, fx["rows"]), dt, device)
+    if fx is not None:
+        fixture_rows = torch.as_tensor(fx["rows"], device=device)
+        x[fixture_rows] = _tensor(C.logical_x_rows(case, fx["rows"]), dt, device)
     if world == 1 or rank == 0:
         w1b, w2b = C.weights(case)
         w1, w2 = _tensor(w1b, dt, device), _tensor(w2b, dt, device)
@@ -562,9 +568,9 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     case = C.get_case(args.workload)
-    p, x, w1, w2, fx = case_inputs(case, dev, world, rank)
+    p, x, w1, w2, fx = case_inputs(case, dev, world, rank, args.rows)
     down = args.down_impl or case.get("down_impl", "basic")
-    fx_rows = [int(r) for r in fx["rows"]]
+    fx_rows = [int(r) for r in fx["rows"]] if fx is not None else []
     burst, sustained, hbm, src = peaks()
     ub = unique_bytes(p, 1 if args.weights == "fp8" else 2)
     flush = args.flush == "on" or (args.flush == "auto" and ub < 2 * L2_BYTES)
@@ -579,7 +585,10 @@ def main():
     torch.cuda.synchronize()
     runner.check()
     y = output()
-    parity = parity_vs_golden(gather_rows(y, owned, fx_rows, p.n, world), fx, p.dtype, fp8=args.weights == "fp8")
+    parity = None
+    if fx is not None:
+        parity = parity_vs_golden(gather_rows(y, owned, fx_rows, p.n, world), fx, p.dtype,
+                                  fp8=args.weights == "fp8")
     runner.check()
     sampler = ClockSampler(local)
     sampler.start()
@@ -661,7 +670,8 @@ def main():
                 st()
             torch.cuda.synchronize()
             r.check()
-            par = parity_vs_golden(gather_rows(outp(), own, fx_rows, p.n, world), fx, p.dtype)
+            yv = outp()
+            par = parity_vs_golden(gather_rows(yv, own, fx_rows, p.n, world), fx, p.dtype) if fx is not None else None
             r.check()
             sync_all(world)
             msv = timed(st, args.steps, scrub)
@@ -700,7 +710,7 @@ def main():
         del ms_r, xh, yh
 
     configs = None
-    if world == 1 and not args.no_per_config and args.workload == "cfg5_bf16":
+    if world == 1 and not args.no_per_config and args.workload == "cfg5_bf16" and args.rows is None:
         if runner is not None:
             close_runner(runner)
             runner = None
