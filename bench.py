@@ -50,6 +50,7 @@ REFERENCE_INSTALL = ROOT / "baseline" / "_ref"
 
 # (workload, down_impl, weights) timed in the per_config block; cfg5 is the headline line.
 PER_CONFIG = [("cfg1_fp16", "basic", "native"), ("cfg1_fp16", "streamk", "native"),
+              ("cfg1_fp16", "full_load_a", "native"),
               ("cfg2_fp16", "streamk", "native"), ("cfg2_fp16", "full_load_a", "native"),
               ("cfg2_bf16", "streamk", "native"), ("cfg2_bf16", "full_load_a", "native"),
               ("cfg3_bf16", "streamk", "native"), ("cfg3_bf16", "streamk", "fp8"),
@@ -72,8 +73,11 @@ def parse():
                     help="override the workload's down_impl")
     ap.add_argument("--weights", choices=("native", "fp8"), default="native",
                     help="fp8: e4m3 weights with per-row scales, widened on chip (decode tiles, M <= 64)")
-    ap.add_argument("--schedule", choices=("static", "dynamic"), default=None,
-                    help="data-parallel tile order (default: dynamic for CTA-pair tiles, static otherwise)")
+    ap.add_argument("--schedule", choices=("static", "dynamic", "static_synced"), default=None,
+                    help="data-parallel tile order (default: dynamic for CTA-pair tiles, static otherwise; "
+                         "static_synced: static with each wave started after every owner started the previous one)")
+    ap.add_argument("--raster-group", type=int, default=None,
+                    help="N=1: tile rows per raster group (default: the planner's balanced choice)")
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--flush", choices=("auto", "on", "off"), default="auto",
                     help="flush L2 between timed steps (auto: when the operands fit in 2x L2)")
@@ -452,6 +456,7 @@ def make_runner(kind, x, w1, w2, down, args, world):
 
     if world == 1:
         r = prepare_ffn(x, w1, w2, down_impl=down, tile=args.tile, schedule=args.schedule,
+                        raster_group=args.raster_group,
                         weight_format=None if args.weights == "native" else args.weights)
         return r, r.run, 1, "single", (lambda g: g), r.run
     if kind in ("hf", "hf_input"):

@@ -30,14 +30,14 @@ GELU_CODES = {"rational": 0, "erf": 1, "silu": 2, "swiglu": 3}  # hidden-layer a
 # Kernel variants selectable through prepare_ffn(..., tile=...) (None = automatic).
 TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pair256x256": 5,
                  "swap16k4": 6, "swap64k2": 7, "rowblock64": 8, "rowblock128": 9, "rowblock256": 10,
-                 "swap16fp8": 11, "swap64fp8": 12}
+                 "swap16fp8": 11, "swap64fp8": 12, "hslice16": 13}
 WEIGHT_FORMATS = {"native": 0, "fp8": 1}
 # Element type of the partial tiles the fused reduce-scatter sends between GPUs.
 PARTIAL_TYPES = {"fp32": 0, "input": 1}
 L2_POLICIES = {"none": 1, "stream_b": 2, "normal": 3, "keep_a": 4}
-SCHEDULES = {"static": 1, "dynamic": 2}
+SCHEDULES = {"static": 1, "dynamic": 2, "static_synced": 3}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",
-                 3: "Stream-K partial wait timed out", 4: "peer GPU partial wait timed out (fused reduce-scatter)",
+                 3: "Stream-K (or cross-cluster) partial wait timed out", 4: "peer GPU partial wait timed out (fused reduce-scatter)",
                  5: "tile claim out of range (counters not reset after an earlier error)",
                  6: "activation beyond the fp16 range of the fp8-weight path (|x| > 65504)"}
 

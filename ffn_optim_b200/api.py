@@ -270,9 +270,11 @@ class PreparedFFN:
             lib.ffn_b200_set_trace(self.handle, None)
         t = stamps.cpu()
         t0 = int(t[:, 0][t[:, 0] > 0].min())
-        names = ("start", "first_load", "down_ready", "last_load", "last_mma", "up_stored", "first_down", "end")
+        names = {0: "start", 1: "first_load", 2: "down_ready", 3: "last_load", 4: "last_mma", 5: "up_stored",
+                 6: "first_down", 7: "end", 9: "aux1", 10: "aux2", 11: "aux3", 12: "aux4", 13: "aux5", 14: "aux6",
+                 15: "aux7"}
         out = {}
-        for i, name in enumerate(names):
+        for i, name in names.items():
             col = t[:, i][t[:, i] > 0].double()
             if col.numel():
                 rel = (col - t0) / 1e3

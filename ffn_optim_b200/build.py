@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 LIBDIR = PKG / "_lib"
 LIB = LIBDIR / "libffn_b200.so"
 SOURCES = [CSRC / "ffn_capi.cu", CSRC / "ffn_noalloc.cu", CSRC / "ffn_placement.cu", CSRC / "ffn_quant.cu"]
-HEADERS = [CSRC / "ffn_kernel.cuh", CSRC / "ffn_rowblock.cuh", ROOT / "include" / "ffn_b200.h"]
+HEADERS = [CSRC / "ffn_kernel.cuh", CSRC / "ffn_rowblock.cuh", CSRC / "ffn_hslice.cuh", ROOT / "include" / "ffn_b200.h"]
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 
 

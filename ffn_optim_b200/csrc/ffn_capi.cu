@@ -11,8 +11,10 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -20,6 +22,7 @@
 #include "../../include/ffn_b200.h"
 #include "ffn_kernel.cuh"
 #include "ffn_rowblock.cuh"
+#include "ffn_hslice.cuh"
 
 namespace ffnb200 {
 const int32_t* internal_pair_owner_map(int device, int grid, int smem);  // ffn_placement.cu
@@ -38,20 +41,25 @@ struct Variant {
   int epi;        // epilogue warps (4, or 8 = two per TMEM sub-partition for short tiles)
   bool rowblock;  // hidden-resident row-block kernel (down_impl full_load_a); bn = Y width
   bool w8;        // fp8 weights widened on chip by 4 converter warps (decode tiles)
+  int hslice;     // hidden-slice decode kernel: cluster size (CTAs sharing a hidden super-block)
 };
 // 0: prefill tiles 128x256 (one CTA), 1: 128x128 for small grids, 2/3: swap-AB decode
 // tiles (16 / 64 tokens), 4: prefill tiles 256x256 computed by a CTA pair (cta_group::2),
 // 5/6: swap-AB decode tiles with 256/128-wide K stages (longer contiguous weight reads),
 // 7/8/9: hidden-resident row blocks with a 64/128/256-column Y accumulator,
-// 10/11: swap-AB decode tiles (16 / 64 tokens) with fp8 weights.
+// 10/11: swap-AB decode tiles (16 / 64 tokens) with fp8 weights, 12: hidden-slice decode
+// (16 tokens; clusters of 2, 4 or 8 CTAs -- the plan's row_split -- each CTA owning 128
+// hidden rows, ffn_hslice.cuh).
+constexpr int kSliceVariant = 12;
 constexpr Variant kVariants[] = {
     {256, 4, false, false, 1, 4, false, false}, {128, 4, false, false, 1, 8, false, false},
     {16, 8, true, false, 1, 8, false, false},   {64, 8, true, false, 1, 8, false, false},
     {256, 6, false, true, 1, 4, false, false},  {16, 3, true, false, 4, 8, false, false},
     {64, 4, true, false, 2, 8, false, false},   {64, 4, false, false, 1, 16, true, false},
     {128, 4, false, false, 1, 16, true, false}, {256, 4, false, false, 1, 16, true, false},
-    {16, 6, true, false, 2, 8, false, true},    {64, 4, true, false, 2, 8, false, true}};
-constexpr int kNumVariants = 12;
+    {16, 6, true, false, 2, 8, false, true},    {64, 4, true, false, 2, 8, false, true},
+    {16, ffnb200::SliceLayout<4>::kStages, true, false, 1, 4, false, false, 4}};
+constexpr int kNumVariants = 13;
 constexpr int kFirstRowblock = 7;
 
 template <int BN, int ST, bool SW, bool PR, int KS, int EP, bool W8, bool B16>
@@ -88,6 +96,30 @@ KernelFn pick_rowblock(int bf16, int act) {
   return act == 2 ? ffn_rowblock_kernel<NY, 4, false, 2>
                   : (act == 1 ? ffn_rowblock_kernel<NY, 4, false, 1> : ffn_rowblock_kernel<NY, 4, false, 0>);
 }
+template <int S>
+KernelFn pick_hslice_s(int bf16, int act) {
+  using namespace ffnb200;
+  if (bf16) {
+    return act == 2 ? ffn_hslice_kernel<S, true, 2>
+                    : (act == 1 ? ffn_hslice_kernel<S, true, 1> : ffn_hslice_kernel<S, true, 0>);
+  }
+  return act == 2 ? ffn_hslice_kernel<S, false, 2>
+                  : (act == 1 ? ffn_hslice_kernel<S, false, 1> : ffn_hslice_kernel<S, false, 0>);
+}
+// Hidden-slice kernels by cluster size S (the plan's row_split); SwiGLU has none.
+KernelFn pick_hslice(int S, int bf16, int act) {
+  if (act == FFN_B200_SWIGLU) return nullptr;
+  return S == 8 ? pick_hslice_s<8>(bf16, act) : (S == 4 ? pick_hslice_s<4>(bf16, act) : pick_hslice_s<2>(bf16, act));
+}
+int hslice_smem(int S) {
+  return S == 8 ? ffnb200::SliceLayout<8>::kSmem
+                : (S == 4 ? ffnb200::SliceLayout<4>::kSmem : ffnb200::SliceLayout<2>::kSmem);
+}
+int hslice_ring_bytes(int S) {
+  return S == 8 ? ffnb200::SliceLayout<8>::kStages * ffnb200::SliceLayout<8>::kStage
+                : (S == 4 ? ffnb200::SliceLayout<4>::kStages * ffnb200::SliceLayout<4>::kStage
+                          : ffnb200::SliceLayout<2>::kStages * ffnb200::SliceLayout<2>::kStage);
+}
 KernelFn kernel_for(int variant, int bf16, int gelu) {
   switch (variant) {
 #define X(id, bn, st, sw, pr, ks, ep, w8) \
@@ -97,6 +129,7 @@ KernelFn kernel_for(int variant, int bf16, int gelu) {
     case 7: return pick_rowblock<64>(bf16, gelu);
     case 8: return pick_rowblock<128>(bf16, gelu);
     case 9: return pick_rowblock<256>(bf16, gelu);
+    case kSliceVariant: return pick_hslice(kVariants[kSliceVariant].hslice, bf16, gelu);
   }
   return nullptr;
 }
@@ -109,6 +142,7 @@ int smem_for(int variant) {
     case 7: return ffnb200::RowLayout<64, 4>::kSmem;
     case 8: return ffnb200::RowLayout<128, 4>::kSmem;
     case 9: return ffnb200::RowLayout<256, 4>::kSmem;
+    case kSliceVariant: return hslice_smem(kVariants[kSliceVariant].hslice);
   }
   return 0;
 }
@@ -122,7 +156,7 @@ int tmem_cols_for(int variant) {
     FFN_B200_VARIANTS(X)
 #undef X
   }
-  return 512;  // row-block variants
+  return 512;  // row-block and hidden-slice variants
 }
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -173,26 +207,29 @@ int phase_plan(const PhaseInput& in, int tile_m, int bn, int tile_k, int C, bool
 
 // down_impl full_load_a: hidden-resident row blocks (ffn_rowblock.cuh).  One CTA per row
 // block of 128 tokens, up to `grid` CTAs; the Y row block lives in TMEM next to the two up
-// accumulators, so it applies when N <= 256 (as the reference's full-load tiling applies
-// only when the operand fits on chip).
+// accumulators, at most 256 columns of it, so it applies when N <= 512 (as the reference's
+// full-load tiling applies only when the operand fits on chip): above 256 columns each row
+// block is computed as two units, one per half of Y, each recomputing the hidden chunks.
 int plan_rowblock(const ffn_b200_problem& pr, int grid, ffn_b200_plan* out) {
-  if (pr.n > 256) return FFN_B200_ERR_NOT_APPLICABLE;
+  if (pr.n > 512) return FFN_B200_ERR_NOT_APPLICABLE;
   int variant = pr.n <= 64 ? kFirstRowblock : (pr.n <= 128 ? kFirstRowblock + 1 : kFirstRowblock + 2);
   if (pr.tile_variant > 0) {
     const int forced = pr.tile_variant - 1;
-    if (!kVariants[forced].rowblock || kVariants[forced].bn < pr.n) return FFN_B200_ERR_INVALID;
+    if (!kVariants[forced].rowblock || 2 * kVariants[forced].bn < pr.n) return FFN_B200_ERR_INVALID;
     variant = forced;
   }
   const Variant& v = kVariants[variant];
   const int64_t rows = cdiv(pr.m, ffnb200::kBM);
+  const int64_t parts = cdiv(pr.n, v.bn);  // Y column parts (1 or 2), one unit each per row block
+  const int64_t units = rows * parts;
   // 128-row chunks of W1: H/128, or for SwiGLU's packed W1 (64 gate + 64 up rows) H/64.
   const int64_t chunks = pr.gelu == FFN_B200_SWIGLU ? cdiv(pr.h, 64) : cdiv(pr.h, 128);
-  if (rows * chunks >= (int64_t(1) << 31)) return FFN_B200_ERR_TOO_LARGE;
-  // Few row blocks: clusters of S CTAs split each block's H chunks (S = 2 or 4 while S*rows
-  // CTAs fit the grid and every CTA keeps at least one chunk); one row block per cluster.
+  if (units * chunks >= (int64_t(1) << 31)) return FFN_B200_ERR_TOO_LARGE;
+  // Few units: clusters of S CTAs split each unit's H chunks (S = 2, 4 or 8 while S*units
+  // CTAs fit the grid and every CTA keeps at least one chunk); one unit per cluster.
   int S = 1;
-  while (S < 4 && rows * S * 2 <= grid && chunks >= S * 2) S *= 2;
-  const int C = static_cast<int>(S > 1 ? rows * S : (rows < grid ? rows : grid));
+  while (S < 8 && units * S * 2 <= grid && chunks >= S * 2) S *= 2;
+  const int C = static_cast<int>(S > 1 ? units * S : (units < grid ? units : grid));
   auto fill = [&](ffn_b200_phase_plan* ph, int64_t tq, int64_t depth) {
     ph->tiles_r = static_cast<int32_t>(rows);
     ph->tiles_q = static_cast<int32_t>(tq);
@@ -213,6 +250,79 @@ int plan_rowblock(const ffn_b200_problem& pr, int grid, ffn_b200_plan* out) {
   out->smem_bytes = smem_for(variant);
   out->workspace_floats = 4;
   out->counter_words = ffnb200::kClaimWords + 2;
+  out->flag_words = 2;
+  out->status_words = 4;
+  out->schedule = 1;
+  out->row_split = S;
+  return FFN_B200_OK;
+}
+
+// Hidden-slice decode plan (ffn_hslice.cuh): M <= 16 tokens; clusters of S CTAs, CTA r of a
+// cluster owning hidden rows [(sb*S + r)*128, +128) of each super-block sb the cluster takes
+// (super-block sb goes to cluster sb mod CL) and Y rows of n-blocks [r*NBR, (r+1)*NBR).
+// Every cluster must be resident at once (the final reduction waits on all of them).  With
+// one CTA per SM a B200 (148 SMs) holds at most 74 / 33 / 15 clusters of 2 / 4 / 8 CTAs
+// (cudaOccupancyMaxActiveClusters, measured; ffn_b200_prepare checks the actual device), so
+// the planner takes the largest S whose super-blocks fit one wave of clusters, else the S
+// with the most even share.  `forced`: chosen through tile_variant; otherwise only when the
+// clusters get equal shares of super-blocks (within 15 %) and there are at least two.
+int plan_hslice(const ffn_b200_problem& pr, int grid, bool forced, ffn_b200_plan* out) {
+  if (pr.m > 16 || pr.gelu == FFN_B200_SWIGLU || pr.weight_format != FFN_B200_WEIGHTS_NATIVE)
+    return FFN_B200_ERR_NOT_APPLICABLE;
+  const int64_t nhb = cdiv(pr.h, ffnb200::kBM);
+  const int64_t nnb = cdiv(pr.n, ffnb200::kBM);
+  const int sm = pr.sm_count > 0 ? pr.sm_count : 148;
+  int best_s = 0;
+  int64_t best_cl = 0;
+  double best_bal = -1.0;
+  for (int S : {8, 4, 2}) {
+    const int64_t cap = (S == 8 ? 15 : (S == 4 ? 33 : 74)) * static_cast<int64_t>(sm) / 148;
+    const int64_t cl_max = std::min<int64_t>(cap, grid / S);
+    const int64_t sb = cdiv(nhb, S);
+    const int64_t nbr = cdiv(nnb, S);
+    if (cl_max < 1) continue;
+    const int64_t cl = std::min(sb, cl_max);
+    if (nbr * 16 > 448) continue;  // down accumulators beside the up one in TMEM
+    const int64_t waves = cdiv(sb, cl);
+    const double bal = static_cast<double>(sb) / static_cast<double>(waves * cl);
+    if (waves == 1) {  // the largest cluster whose super-blocks fit one wave
+      best_s = S; best_cl = cl; best_bal = 1.0;
+      break;
+    }
+    if (bal > best_bal + 1e-9) { best_s = S; best_cl = cl; best_bal = bal; }
+  }
+  if (best_s == 0) return FFN_B200_ERR_NOT_APPLICABLE;
+  const int S = best_s;
+  const int64_t sb = cdiv(nhb, S);
+  const int64_t nbr = cdiv(nnb, S);
+  const int64_t cl = best_cl;
+  if (!forced && (sb < 2 || best_bal < 0.85)) return FFN_B200_ERR_NOT_APPLICABLE;
+  auto fill = [](ffn_b200_phase_plan* ph, int64_t tiles, int64_t depth) {
+    ph->tiles_r = static_cast<int32_t>(tiles);
+    ph->tiles_q = 1;
+    ph->tiles = static_cast<int32_t>(tiles);
+    ph->k_blocks = static_cast<int32_t>(cdiv(depth, ffnb200::kBK));
+    ph->dp_tiles = ph->tiles;
+    ph->sk_tiles = 0;
+    ph->sk_iters = 0;
+    ph->sk_rem = 0;
+    ph->group = 1;
+    ph->sk_ctas = 0;
+  };
+  fill(&out->up, nhb, pr.k);
+  fill(&out->down, nnb, pr.h);
+  out->variant = kSliceVariant;
+  out->swap_ab = 1;
+  out->cta_pair = 0;
+  out->tile_m = ffnb200::kBM;
+  out->tile_n = kVariants[kSliceVariant].bn;
+  out->tile_k = ffnb200::kBK;
+  out->stages = hslice_ring_bytes(S) / ffnb200::SliceLayout<4>::kStage;
+  out->block_num = static_cast<int32_t>(cl * S);
+  out->tmem_cols = tmem_cols_for(kSliceVariant);
+  out->smem_bytes = hslice_smem(S);
+  out->workspace_floats = cl * S * nbr * ffnb200::kBM * 16;  // one fp32 [S*NBR*128 x 16] partial per cluster
+  out->counter_words = ffnb200::kClaimWords + S;              // one count per cluster rank
   out->flag_words = 2;
   out->status_words = 4;
   out->schedule = 1;
@@ -356,7 +466,7 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   if (grid < 1 || grid > 65535 || pr->block_num < 0) return FFN_B200_ERR_INVALID;
   if (pr->tile_variant < 0 || pr->tile_variant > kNumVariants) return FFN_B200_ERR_INVALID;
   if (pr->raster_group < 0 || pr->l2_policy < 0 || pr->l2_policy > 4) return FFN_B200_ERR_INVALID;
-  if (pr->schedule < 0 || pr->schedule > 2) return FFN_B200_ERR_INVALID;
+  if (pr->schedule < 0 || pr->schedule > 3) return FFN_B200_ERR_INVALID;
   if (pr->weight_format != FFN_B200_WEIGHTS_NATIVE && pr->weight_format != FFN_B200_WEIGHTS_FP8_ROWS)
     return FFN_B200_ERR_INVALID;
   const bool fp8w = pr->weight_format == FFN_B200_WEIGHTS_FP8_ROWS;
@@ -372,8 +482,12 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   // HBM-bound regime where halving the weight bytes matters).
   if (fp8w && pr->tile_variant == 0 && pr->m > 64) return FFN_B200_ERR_NOT_APPLICABLE;
   if (fp8w && ((pr->k & 1) || (pr->h & 1))) return FFN_B200_ERR_NOT_APPLICABLE;  // code pairs per TMA element
+  const bool slice_forced = pr->tile_variant == kSliceVariant + 1;
   int variant;
-  if (pr->tile_variant > 0) {
+  if (slice_forced) {
+    variant = 2;  // the swap-AB plan's applicability rules come first
+    if (pr->m > 16) return FFN_B200_ERR_INVALID;
+  } else if (pr->tile_variant > 0) {
     variant = pr->tile_variant - 1;
     if (kVariants[variant].swap && pr->m > kVariants[variant].bn) return FFN_B200_ERR_INVALID;
     if (kVariants[variant].pair && grid < 2) return FFN_B200_ERR_INVALID;
@@ -455,6 +569,14 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   // or two waves, where a claim would only add its latency.
   out->schedule = pr->schedule ? pr->schedule : (v.pair ? 2 : 1);
   out->row_split = 1;
+  // Decode (M <= 16): the hidden-slice kernel where its clusters share the work evenly.
+  if (slice_forced || (pr->tile_variant == 0 && variant == 2)) {
+    ffn_b200_plan sl;
+    std::memset(&sl, 0, sizeof(sl));
+    const int rs = plan_hslice(*pr, grid, slice_forced, &sl);
+    if (rs == FFN_B200_OK) *out = sl;
+    else if (slice_forced) return rs == FFN_B200_ERR_NOT_APPLICABLE ? FFN_B200_ERR_INVALID : rs;
+  }
   return FFN_B200_OK;
 }
 
@@ -507,7 +629,8 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   h->plan = plan;
   h->buf = *b;
   h->device = device;
-  h->kernel = kernel_for(plan.variant, prob.dtype == FFN_B200_BF16, prob.gelu);
+  h->kernel = kVariants[plan.variant].hslice ? pick_hslice(plan.row_split, prob.dtype == FFN_B200_BF16, prob.gelu)
+                                             : kernel_for(plan.variant, prob.dtype == FFN_B200_BF16, prob.gelu);
 
   Params& P = h->params;
   std::memset(&P, 0, sizeof(P));
@@ -580,6 +703,15 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   const int ncta = plan.cta_pair ? 2 : 1;
   P.C = plan.block_num / ncta;
   P.rb_split = plan.row_split;
+  // Serpentine K order for the prefill tiles (cfg5: DRAM reads 60.6 -> 53.2 GB per call, +1 %
+  // TFLOP/s at a 2 % higher clock under the power cap); decode tiles stream weights once.
+  P.kserp = plan.swap_ab ? 0 : 1;
+  P.wave_sync = plan.schedule == 3 ? 1 : 0;
+  if (kVariants[plan.variant].hslice) {
+    const int S = plan.row_split;
+    P.hs_superblocks = static_cast<int>(cdiv(plan.up.tiles_r, S));
+    P.hs_nbr = static_cast<int>(cdiv(plan.down.tiles_r, S));
+  }
   P.wait_limit_ns = 4000000000ull;
   P.inject = 0;
   P.l2_hints = prob.l2_policy == 2 ? 1 : (prob.l2_policy == 3 ? 2 : (prob.l2_policy == 4 ? 3 : 0));
@@ -593,9 +725,11 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
   const cudaError_t e =
       cudaFuncSetAttribute(h->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem_bytes));
   int rc2 = e == cudaSuccess ? FFN_B200_OK : FFN_B200_ERR_CUDA;
-  if (!rc2 && plan.cta_pair) {
-    // Every CTA pair of the persistent grid must be resident at once (the down phase waits
-    // on up tiles of other pairs): the grid may not exceed the co-resident cluster count.
+  const int wait_cluster = plan.cta_pair ? 2 : (kVariants[plan.variant].hslice ? plan.row_split : 1);
+  if (!rc2 && wait_cluster > 1) {
+    // Every cluster of the grid must be resident at once (pairs: the down phase waits on up
+    // tiles of other pairs; hidden slices: the final reduction waits on every cluster): the
+    // grid may not exceed the co-resident cluster count.
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(static_cast<unsigned>(plan.block_num), 1, 1);
@@ -603,7 +737,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     cfg.dynamicSmemBytes = static_cast<size_t>(plan.smem_bytes);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(wait_cluster);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
@@ -612,7 +746,7 @@ int ffn_b200_prepare(const ffn_b200_problem* pr, const ffn_b200_buffers* b, int 
     if (cudaOccupancyMaxActiveClusters(&clusters, h->kernel, &cfg) != cudaSuccess) {
       cudaGetLastError();
       rc2 = FFN_B200_ERR_CUDA;
-    } else if (plan.block_num > 2 * clusters) {
+    } else if (plan.block_num > wait_cluster * clusters) {
       rc2 = FFN_B200_ERR_DEVICE;
     }
   }
@@ -883,6 +1017,7 @@ int ffn_b200_launch(const ffn_b200_problem* pr, const ffn_b200_buffers* b, void*
 // Internal accessors used by the allocation-free entry point in ffn_noalloc.cu; not exported.
 namespace ffnb200 {
 bool internal_is_rowblock(int variant) { return variant >= 0 && variant < kNumVariants && kVariants[variant].rowblock; }
+bool internal_is_hslice(int variant) { return variant >= 0 && variant < kNumVariants && kVariants[variant].hslice > 0; }
 void (*internal_kernel_for(int variant, int bf16, int gelu))(const Params) {
   return kernel_for(variant, bf16, gelu);
 }

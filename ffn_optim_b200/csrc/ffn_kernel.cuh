@@ -101,6 +101,10 @@ struct Params {
   // rs_fp32 = 0) into that rank's staging buffer over NVLink; an owner sums the partials of
   // its band in ascending rank order.
   int rb_split;          // row-block kernel: CTAs (a cluster) sharing one row block's H chunks
+  int kserp;             // 1: serpentine K order over the waves of data-parallel tiles (see the producer)
+  int wave_sync;         // 1 (static schedule): an owner starts wave i once every owner started wave i - 1
+  int hs_superblocks;    // hidden-slice decode kernel: super-blocks of (cluster size) x 128 hidden rows
+  int hs_nbr;            // hidden-slice decode kernel: 128-row blocks of Y per cluster rank
   int rs_world, rs_rank, rs_band_tiles;
   int rs_fp32;                     // 1: staged partials are fp32; 0: the input dtype
   void* rs_stage[kMaxRanks];       // per rank: [2 parity][world][band tiles][kBM][BN] partials
@@ -125,6 +129,9 @@ enum TraceSlot : int {
   kTrFirstDown = 6,   // first epilogue warp got its first down-phase accumulator
   kTrEnd = 7,         // teardown reached
   kTrSmid = 8,        // not a stamp: the SM (%smid) the CTA ran on
+  kTrAux1 = 9,        // kernel-specific stamps (hidden-slice kernel: all partials released,
+  kTrAux2 = 10,       // reduction pieces landed, Y written)
+  kTrAux3 = 11,
   kTrWords = 16       // words per CTA
 };
 
@@ -438,6 +445,52 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 64 consecutive 32-bit columns of this warp's 32 lanes, with the wait in the same asm block.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Two 16-column loads at different column addresses, one wait (in the same asm block, so the
+// outputs are never consumed before they have landed).
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(ta), "r"(tb)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[16 + i]);
+  }
+}
+
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
   uint32_t r[8];
   asm volatile(
@@ -638,6 +691,7 @@ struct Unit {
   int kb0, kb1;  // k-block range
   int role;      // kRoleFull / kRoleOwner / kRoleContrib
   int c_first, c_last;  // contributors whose partials an owner adds (ascending)
+  int rev;       // 1: the producer loads the k-blocks in descending order
 };
 
 __device__ __forceinline__ int sk_start(const PhaseSched& s, int c) { return c * s.q + min(c, s.rem); }
@@ -668,7 +722,7 @@ __device__ __forceinline__ void unit_coords(const Params& p, const Unit& u, int&
 // Data-parallel tile t of a phase: the whole K range in one unit.
 __device__ __forceinline__ void dp_unit(const PhaseSched& s, int ph, int t, Unit& u) {
   u.phase = ph; u.tile = t; u.kb0 = 0; u.kb1 = s.L;
-  u.role = kRoleFull; u.c_first = 1; u.c_last = 0;
+  u.role = kRoleFull; u.c_first = 1; u.c_last = 0; u.rev = 0;
 }
 // Stream-K part `idx` of owner c in a phase (static split of the tail tiles' K blocks).
 __device__ __forceinline__ bool sk_unit(const PhaseSched& s, int ph, int c, int idx, Unit& u) {
@@ -681,7 +735,7 @@ __device__ __forceinline__ bool sk_unit(const PhaseSched& s, int ph, int c, int 
   const int trel = st / s.L + idx;
   const int tb = trel * s.L, te = tb + s.L;
   const int a = max(st, tb), b = min(en, te);
-  u.phase = ph; u.tile = s.dp + trel; u.kb0 = a - tb; u.kb1 = b - tb;
+  u.phase = ph; u.tile = s.dp + trel; u.kb0 = a - tb; u.kb1 = b - tb; u.rev = 0;
   if (a == tb) {
     u.role = kRoleOwner; u.c_first = c + 1; u.c_last = sk_cta_of(s, te - 1);
   } else {
@@ -689,14 +743,14 @@ __device__ __forceinline__ bool sk_unit(const PhaseSched& s, int ph, int c, int 
   }
   return true;
 }
-// A unit as the 8 words of a unit-ring slot; word 7 = 1 for a unit, 0 for end of work.
+// A unit as the 8 words of a unit-ring slot; word 7 = 1 + rev for a unit, 0 for end of work.
 __device__ __forceinline__ void pack_unit(const Unit& u, int* w) {
   w[0] = u.phase; w[1] = u.tile; w[2] = u.kb0; w[3] = u.kb1;
-  w[4] = u.role; w[5] = u.c_first; w[6] = u.c_last; w[7] = 1;
+  w[4] = u.role; w[5] = u.c_first; w[6] = u.c_last; w[7] = 1 + u.rev;
 }
 __device__ __forceinline__ void unpack_unit(const int* w, Unit& u) {
   u.phase = w[0]; u.tile = w[1]; u.kb0 = w[2]; u.kb1 = w[3];
-  u.role = w[4]; u.c_first = w[5]; u.c_last = w[6];
+  u.role = w[4]; u.c_first = w[5]; u.c_last = w[6]; u.rev = w[7] - 1;
 }
 
 __device__ __forceinline__ void trace_mark(const Params& p, int slot) {
@@ -1039,7 +1093,11 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             mbar_expect_tx(full_bar(st), LY::kStageBytes);
           }
         };
-        int kb = u.kb0;
+        // K-block of step j: ascending, or descending for a reversed unit (the MMA adds the
+        // stages in the order they arrive; it never reads the k-block index).
+        auto kb_at = [&](int j) { return u.rev ? u.kb1 - 1 - j : u.kb0 + j; };
+        const int nk = u.kb1 - u.kb0;
+        int j0 = 0;
         if (u.phase == 1) {
           const int blk = SWAP ? tq : tr;
           if (blk != ready_blk) {
@@ -1049,13 +1107,13 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             // hidden operand.  (An extra L2 prefetch of W2 here was measured neutral on the
             // bandwidth-bound decode shape: it only moved bytes from the down to the up phase.)
             const int wop = SWAP ? 0 : 1;
-            const int n_pre = min(STAGES, u.kb1 - u.kb0);
+            const int n_pre = min(STAGES, nk);
             const int st0 = stage;
             int pre = 0;
             for (; pre < n_pre; ++pre) {
               if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) return false;
               arm(stage);
-              load(wop, stage, kb + pre);
+              load(wop, stage, kb_at(pre));
               if (issued == 0) trace_mark(p, kTrFirstLoad);
               ++issued;
               if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -1064,16 +1122,16 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             fence_async_global();
             if (ready_blk < 0) trace_mark(p, kTrDownReady);
             ready_blk = blk;
-            for (int j = 0; j < pre; ++j) load(1 - wop, (st0 + j) % STAGES, kb + j);
-            kb += pre;
+            for (int j = 0; j < pre; ++j) load(1 - wop, (st0 + j) % STAGES, kb_at(j));
+            j0 = pre;
           }
         }
 #pragma unroll 1
-        for (; kb < u.kb1; ++kb) {
+        for (int j = j0; j < nk; ++j) {
           if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p, 100 + stage)) return false;
           arm(stage);
-          load(0, stage, kb);
-          load(1, stage, kb);
+          load(0, stage, kb_at(j));
+          load(1, stage, kb_at(j));
           if (issued == 0) trace_mark(p, kTrFirstLoad);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -1127,8 +1185,40 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
               break;
             }
             if (t >= s.dp) break;
+            if (p.wave_sync && !p.dyn) {
+              // Static order with bounded drift: start wave i = t / C only once every owner has
+              // started its tile of wave i - 1 (the phase's started-tile count, claims[ph],
+              // grows by exactly dp per launch), so owners that share operand strips stay
+              // within one tile of each other.
+              if (!need_epoch()) { ok = false; break; }
+              const long long wave = t / p.C;
+              if (wave > 0) {
+                const unsigned long long want =
+                    (epoch - 1ull) * static_cast<unsigned long long>(s.dp) + static_cast<unsigned long long>(wave * p.C);
+                const uint64_t t0 = gtimer();
+                uint32_t n = 0;
+#pragma unroll 1
+                while (static_cast<long long>(*reinterpret_cast<volatile unsigned long long*>(p.claims + ph) - want) < 0) {
+                  __nanosleep(128);
+                  if ((++n & 15u) == 0) {
+                    if (*abort_flag) { ok = false; break; }
+                    if (gtimer() - t0 > p.wait_limit_ns) {
+                      report(p, 2, 1000 + ph);
+                      *abort_flag = 1;
+                      ok = false;
+                      break;
+                    }
+                  }
+                }
+                if (!ok) break;
+              }
+              atomicAdd(p.claims + ph, 1ull);
+            }
             Unit u;
             dp_unit(s, ph, static_cast<int>(t), u);
+            // Serpentine K order: the data-parallel tiles of every other wave walk K backwards,
+            // so a wave starts on the K-slices the previous wave (the same rows) left in L2.
+            u.rev = p.kserp && ((t / p.C) & 1) ? 1 : 0;
             int w[8];
             pack_unit(u, w);
             if (!publish(w)) { ok = false; break; }

@@ -35,6 +35,7 @@ int internal_encode_2d(CUtensorMap* tm, const void* base, int dtype, int64_t inn
                        uint32_t box_inner, uint32_t box_outer);
 int internal_threads_for(int variant);
 bool internal_is_rowblock(int variant);
+bool internal_is_hslice(int variant);
 }  // namespace ffnb200
 
 // The scratch.  In host code this name is only a stand-in for the symbol; the device address
@@ -91,7 +92,7 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   ffn_b200_problem prob = *problem;
   prob.sm_count = sm;
   if (prob.block_num > sm) return FFN_B200_ERR_DEVICE;
-  if (prob.tile_variant == 5) return FFN_B200_ERR_INVALID;  // CTA-pair tiles need a cluster launch
+  if (prob.tile_variant == 5 || prob.tile_variant == 13) return FFN_B200_ERR_INVALID;  // cluster-launched tiles
   if (prob.weight_format != FFN_B200_WEIGHTS_NATIVE) return FFN_B200_ERR_INVALID;  // no scale arguments here
   // SwiGLU's W1 row order depends on the chosen tiles, which this entry point may change.
   if (prob.gelu == FFN_B200_SWIGLU) return FFN_B200_ERR_INVALID;
@@ -100,6 +101,11 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   if (rc) return rc;
   if (plan.cta_pair) {  // automatic choice of CTA-pair tiles: use the one-CTA 128x256 tiles here
     prob.tile_variant = 1;
+    rc = ffn_b200_make_plan(&prob, &plan);
+    if (rc) return rc;
+  }
+  if (internal_is_hslice(plan.variant)) {  // automatic hidden-slice decode: the swap-AB 16-token tiles here
+    prob.tile_variant = 3;
     rc = ffn_b200_make_plan(&prob, &plan);
     if (rc) return rc;
   }
@@ -168,6 +174,7 @@ extern "C" int ffn_b200_run_noalloc(const ffn_b200_problem* problem, const void*
   P.up = to_sched(plan.up);
   P.dn = to_sched(plan.down);
   P.rb_split = plan.row_split;
+  P.kserp = plan.swap_ab ? 0 : 1;  // the same K order as a prepared handle
   P.M = static_cast<int>(prob.m);
   P.H = static_cast<int>(prob.h);
   P.N = static_cast<int>(prob.n);

@@ -15,15 +15,20 @@
 // up(0) up(1) down(0) up(2) down(1) ... down(J-1).  Hidden never reaches global memory and
 // no CTA waits on another, so the launch needs no co-residency.  TMEM holds both up
 // accumulators (256 columns) and the Y accumulator (NY <= 256 columns): the variant
-// applies when N <= 256.
+// applies when N <= 2 * NY (see the Y column parts below).
+//
+// Y wider than the accumulator (NY < N <= 2*NY): the Y columns are split into NS = ceil(N/NY)
+// parts, and a row unit (row block, part) computes Y[rb, part*NY : part*NY + NY]; each part
+// recomputes the row block's hidden chunks (the up work is done NS times), which keeps both
+// parts free of any exchange.  Units are dealt to CTAs (or clusters) like row blocks.
 //
 // Arithmetic is that of the two-phase kernel: fp32 accumulation over K, GELU of the fp32
 // sum, hidden rounded once to the input dtype, fp32 accumulation over H, one rounding of
 // Y.  Only the order of the H summation differs (chunks of 128 in ascending order, inside
 // one accumulator).
 //
-// Few row blocks (M <= 128 * SMs / 2): a cluster of S = Params::rb_split CTAs shares each
-// row block, CTA s taking H chunks [s*J/S, (s+1)*J/S), so S times as many SMs work and
+// Few row blocks (M <= 128 * SMs / 2): a cluster of S = Params::rb_split CTAs (2, 4 or 8)
+// shares each row block, CTA s taking H chunks [s*J/S, (s+1)*J/S), so S times as many SMs work and
 // each walks 1/S of the chain.  At the end every CTA leaves the fp32 Y partials of the
 // column chunks it does not finalise in its own (then idle) operand ring; Y column chunk yc is finalised by CTA yc % S, which after
 // a cluster barrier reads the other CTAs' partials of it over distributed shared memory and
@@ -88,6 +93,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int RB = p.up.tiles_r;   // row blocks
+  const int NS = (p.N + NY - 1) / NY;  // Y column parts
+  const int units = RB * NS;     // (row block, Y part) units
   const int J = p.up.tiles_q;    // H chunks
   const int KB = p.up.L;         // 64-wide k-blocks of K
   // H split: CTA `srank` of a cluster of S takes chunks [j0, j0 + Js) of its row block.
@@ -95,8 +102,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
   const int srank = S > 1 ? static_cast<int>(cluster_rank()) : 0;
   const int j0 = srank * J / S;
   const int Js = (srank + 1) * J / S - j0;
-  const int rb_first = static_cast<int>(blockIdx.x) / S;
-  const int rb_step = static_cast<int>(gridDim.x) / S;
+  const int un_first = static_cast<int>(blockIdx.x) / S;
+  const int un_step = static_cast<int>(gridDim.x) / S;
 
   if (threadIdx.x == 0) {
 #pragma unroll 1
@@ -153,7 +160,9 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       };
 #pragma unroll 1
-      for (int rb = rb_first; rb < RB && ok; rb += rb_step) {
+      for (int un = un_first; un < units && ok; un += un_step) {
+        const int rb = un / NS;
+        const int ycol0 = (un % NS) * NY;
 #pragma unroll 1
         for (int jj = 0; jj <= Js && ok; ++jj) {
           const int j = j0 + jj;
@@ -174,7 +183,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
             for (int kk = 0; kk < kHidKb; ++kk) {
               if (!next_stage()) { ok = false; break; }
               mbar_expect_tx(full_bar(stage), kDnBytes);
-              tma_load_2d(sS + stage * LY::kStage, &p.tm_b_dn, ((j - 1) * kHidKb + kk) * kBK, 0, full_bar(stage));
+              tma_load_2d(sS + stage * LY::kStage, &p.tm_b_dn, ((j - 1) * kHidKb + kk) * kBK, ycol0, full_bar(stage));
               advance();
             }
           }
@@ -246,7 +255,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         return true;
       };
 #pragma unroll 1
-      for (int rb = rb_first; rb < RB && ok; rb += rb_step) {
+      for (int un = un_first; un < units && ok; un += un_step) {
 #pragma unroll 1
         for (int jj = 0; jj <= Js && ok; ++jj) {
           if (jj < Js && !up_chunk()) ok = false;
@@ -298,7 +307,9 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
       }
     };
 #pragma unroll 1
-    for (int rb = rb_first; rb < RB && ok; rb += rb_step) {
+    for (int un = un_first; un < units && ok; un += un_step) {
+      const int rb = un / NS;
+      const int ycol0 = (un % NS) * NY;
 #pragma unroll 1
       for (int jj = 0; jj < Js && ok; ++jj) {
         const int j = j0 + jj;
@@ -358,26 +369,11 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
       // Y of the row block: 64-column chunks, one per warp of a sub-partition (NY <= 256).
       ok = warp_wait(yfull, rcnt & 1, 440);
       if (!ok) break;
+      if (ew == 0 && lane == 0) trace_mark(p, kTrFirstDown);  // (the last unit's stamp stays)
       tc_fence_after();
       const int yc = part;
-      const bool mine = yc < NY / 64 && yc * 64 < p.N;
-      if (S > 1) {
-        // Split row block (one per cluster): Y chunk yc is finalised by CTA yc % S; the other
-        // CTAs park their partial of it in their operand ring, read after the cluster barrier.
-        if (mine && yc % S != srank) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float v[32];
-            tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), v);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint32_t addr = sS + static_cast<uint32_t>((((ew * 2 + h) * 8 + q) * 32 + lane) * 16);
-              asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[4 * q]), "f"(v[4 * q + 1]),
-                           "f"(v[4 * q + 2]), "f"(v[4 * q + 3])
-                           : "memory");
-            }
-          }
-        }
+      const bool mine = yc < NY / 64 && ycol0 + yc * 64 < p.N;
+      if (S > 1) {  // split row block (one per cluster): combined after the loop
         ++rcnt;
         break;
       }
@@ -386,7 +382,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         for (int h = 0; h < 2; ++h) {
           float v[32];
           tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), v);
-          if (p.bias2) add_bias<BF16, 32>(v, p.bias2, yc * 64 + h * 32, p.N);
+          if (p.bias2) add_bias<BF16, 32>(v, p.bias2, ycol0 + yc * 64 + h * 32, p.N);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
@@ -400,7 +396,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
         fence_async_shared();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&p.tm_st_y, ystage, yc * 64, rb * kBM + sub * 32);
+          tma_store_2d(&p.tm_st_y, ystage, ycol0 + yc * 64, rb * kBM + sub * 32);
           bulk_commit();
         }
       }
@@ -417,62 +413,115 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 16, 1) ffn_rowblock_kernel
   }
 
   if (S > 1) {
+    // Split row block: Y columns [g*GW, (g+1)*GW) of the unit (GW = NY/S, in 8-column units)
+    // are finalised by CTA g of the cluster.  (1) Once every CTA's MMAs are done, the operand
+    // rings are idle; each CTA stores the fp32 partial of every other CTA's columns straight
+    // into that CTA's ring (slot = sender rank; [8-column unit][2 float4][128 rows]), (2) then
+    // each finaliser adds the S partials in rank order (its own from TMEM) and stores Y.
+    constexpr int kUnits = NY / 8;           // 8-column units of the Y accumulator
+    const int gw_units = kUnits / S;          // units per finalising CTA
     tc_fence_before();
-    cluster_sync();  // (1) every peer's Y partial is in its shared memory
+    cluster_sync();  // (1) every CTA of the cluster has its final Y partial in TMEM
     tc_fence_after();
-    const int rb = rb_first;
+    if (threadIdx.x == 0) trace_mark(p, kTrAux1);
+    const int un = un_first;  // one unit per cluster
+    const int rb = un / NS;
+    const int ycol0 = (un % NS) * NY;
     const int ew = warp - kCtrlThreads / 32;
-    if (warp >= kCtrlThreads / 32 && rb < RB && !*abort_flag) {
-      const int sub = warp & 3;
-      const int part = ew >> 2;
-      const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
-      const uint32_t ystage = sH + static_cast<uint32_t>(ew * 4096);
-      const int yc = part;
-      if (yc < NY / 64 && yc * 64 < p.N && yc % S == srank) {  // the Y chunks this CTA finalises
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          float v[32];
-#pragma unroll 1
-          for (int s2 = 0; s2 < S; ++s2) {  // partials summed in rank order
-            float t[32];
-            if (s2 == srank) {
-              tmem_ld32(tmem_base + lane_off + 256u + static_cast<uint32_t>(yc * 64 + h * 32), t);
-            } else {
+    const bool epi = warp >= kCtrlThreads / 32 && un < units && !*abort_flag;
+    const int sub = warp & 3;
+    const int part = ew >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const int row = sub * 32 + lane;
+    auto slot_addr = [&](int sender, int u_local, int half) {  // in the finaliser's ring
+      return sS + static_cast<uint32_t>((((sender * gw_units + u_local) * 2 + half) * kBM + row) * 16);
+    };
+    if (epi) {
+      // Part `part` of the epilogue warps pushes the contiguous units [part*kQ, (part+1)*kQ)
+      // of its 32 rows, read from TMEM in one round trip.
+      constexpr int kQ = kUnits / 4;
+      float v[kQ * 8];
+      const uint32_t tcol = tmem_base + lane_off + 256u + static_cast<uint32_t>(part * kQ * 8);
+      if constexpr (kQ == 8) tmem_ld64(tcol, v);
+      else if constexpr (kQ == 4) tmem_ld32(tcol, v);
+      else tmem_ld16(tcol, v);
+      if (threadIdx.x == kCtrlThreads) trace_mark(p, 12);
 #pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const uint32_t addr = sS + static_cast<uint32_t>((((ew * 2 + h) * 8 + q) * 32 + lane) * 16);
-                const float4 f = ld_cluster_f4(map_to_rank(addr, static_cast<uint32_t>(s2)));
-                t[4 * q] = f.x; t[4 * q + 1] = f.y; t[4 * q + 2] = f.z; t[4 * q + 3] = f.w;
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = s2 == 0 ? t[i] : v[i] + t[i];
-          }
-          if (p.bias2) add_bias<BF16, 32>(v, p.bias2, yc * 64 + h * 32, p.N);
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t addr = ystage + lane * 128 + (((h * 4 + c) ^ (lane & 7)) << 4);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
-                         "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
-                         : "memory");
-          }
-        }
-        fence_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&p.tm_st_y, ystage, yc * 64, rb * kBM + sub * 32);
-          bulk_commit();
-          bulk_wait_read0();
-        }
-        __syncwarp();
+      for (int k = 0; k < kQ; ++k) {
+        const int u = part * kQ + k;
+        const int g = u / gw_units;
+        if (g == srank || ycol0 + u * 8 >= p.N) continue;
+        const uint32_t dst = map_to_rank(slot_addr(srank, u - g * gw_units, 0), static_cast<uint32_t>(g));
+        asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(v[8 * k]), "f"(v[8 * k + 1]),
+                     "f"(v[8 * k + 2]), "f"(v[8 * k + 3])
+                     : "memory");
+        asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst + kBM * 16), "f"(v[8 * k + 4]),
+                     "f"(v[8 * k + 5]), "f"(v[8 * k + 6]), "f"(v[8 * k + 7])
+                     : "memory");
       }
     }
     tc_fence_before();
-    cluster_sync();  // (2) no CTA leaves before the others have read its parked partials
+    cluster_sync();  // (2) every partial is in its finaliser's shared memory; no more remote stores
+    tc_fence_after();
+    if (threadIdx.x == 0) trace_mark(p, kTrAux2);
+    // Finalisation: this CTA's units [srank*gw, (srank+1)*gw), `per` contiguous units per part
+    // (its own partial read from TMEM in one round trip), summed with the S-1 pushed partials
+    // in rank order.
+    const int per = gw_units >= 4 ? gw_units / 4 : 1;
+    const int ul0 = part * per;
+    if (epi && ul0 < gw_units) {
+      uint16_t* y = reinterpret_cast<uint16_t*>(p.y);
+      const long long grow = static_cast<long long>(rb) * kBM + row;  // token row of Y
+      float own[32];
+      const uint32_t tcol = tmem_base + lane_off + 256u + static_cast<uint32_t>((srank * gw_units + ul0) * 8);
+      if (per >= 4) tmem_ld32(tcol, own);
+      else if (per == 2) tmem_ld16(tcol, own);
+      else tmem_ld8(tcol, own);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (k >= per) break;
+        const int ul = ul0 + k;
+        const int u = srank * gw_units + ul;
+        const int col = ycol0 + u * 8;
+        if (col >= p.N) continue;
+        float v[8];
+#pragma unroll 1
+        for (int s2 = 0; s2 < S; ++s2) {  // partials summed in rank order
+          float t[8];
+          if (s2 == srank) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) t[i] = own[8 * k + i];
+          } else {
+            const uint32_t a = slot_addr(s2, ul, 0);
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(t[0]), "=f"(t[1]), "=f"(t[2]), "=f"(t[3]) : "r"(a)
+                         : "memory");
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(t[4]), "=f"(t[5]), "=f"(t[6]), "=f"(t[7])
+                         : "r"(a + kBM * 16)
+                         : "memory");
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = s2 == 0 ? t[i] : v[i] + t[i];
+        }
+        if (threadIdx.x == kCtrlThreads) trace_mark(p, 13);
+        if (p.bias2) add_bias<BF16, 8>(v, p.bias2, col, p.N);
+        if (grow < p.M) {
+          uint16_t* dst = y + grow * p.ldy + col;
+          if (col + 8 <= p.N) {
+            uint4 w;
+            w.x = pack2<BF16>(v[0], v[1]); w.y = pack2<BF16>(v[2], v[3]);
+            w.z = pack2<BF16>(v[4], v[5]); w.w = pack2<BF16>(v[6], v[7]);
+            *reinterpret_cast<uint4*>(dst) = w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (col + i < p.N) dst[i] = cvt1<BF16>(v[i]);
+          }
+        }
+      }
+    }
   }
+  if (threadIdx.x == kCtrlThreads) trace_mark(p, kTrAux3);  // first epilogue warp done
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

@@ -11,7 +11,7 @@ from dataclasses import dataclass
 DOWN_IMPLS = ("basic", "full_load_a", "full_load_b", "streamk")
 KERNEL_ENTRIES = {"basic": "ffn_fused_kernel (down: data-parallel tiles)",
                   "streamk": "ffn_fused_kernel (down: data-parallel waves + Stream-K tail)",
-                  "full_load_a": "ffn_rowblock_kernel (hidden row block resident on chip, N <= 256)"}
+                  "full_load_a": "ffn_rowblock_kernel (hidden row block resident on chip, N <= 512)"}
 
 
 class DependencyUnavailable(RuntimeError):
@@ -27,7 +27,7 @@ class Selection:
     """Up/down implementation names (reference dispatch.py:42-66).
 
     ``up_impl`` must be 'basic'; ``down_impl`` one of :data:`DOWN_IMPLS`.  'full_load_a'
-    (hidden row block resident on chip) applies when N <= 256 and otherwise raises
+    (hidden row block resident on chip) applies when N <= 512 and otherwise raises
     :class:`NotApplicable` at planning; 'full_load_b' raises :class:`DependencyUnavailable`
     from :meth:`require_available`.
     """

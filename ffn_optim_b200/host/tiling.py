@@ -110,7 +110,7 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
     ``block_num`` None means one CTA per SM.  ``tile`` None picks the kernel variant
     automatically; a name of ``_lib.TILE_VARIANTS`` forces one (tests, benchmarks).
     ``raster_group`` (tile rows per raster group), ``l2_policy`` ('none' | 'stream_b' | ...)
-    and ``schedule`` ('static' | 'dynamic' data-parallel tile order) override the
+    and ``schedule`` ('static' | 'dynamic' | 'static_synced' data-parallel tile order) override the
     automatic tuning; ``weight_format='fp8'`` plans the fp8-weight decode tiles (M <= 64,
     otherwise NotApplicable).  Raises
     DependencyUnavailable for the full-load variants, NotApplicable for Stream-K without a
@@ -146,7 +146,7 @@ def make_plan(problem, selection=Selection(), block_num=None, *, gelu="rational"
         if weight_format == "fp8":
             raise NotApplicable("fp8 weights: decode tiles only (M <= 64, even K and H, down_impl basic or streamk)")
         if selection.down_impl == "full_load_a":
-            raise NotApplicable("full_load_a keeps a 128 x N fp32 row block in TMEM: needs N <= 256")
+            raise NotApplicable("full_load_a keeps a 128 x N fp32 row block in TMEM: needs N <= 512 (two 256-column halves)")
         raise NotApplicable("Stream-K candidate has no remainder tiles for this block_num "
                             "or fewer than two K tiles")
     if rc == _lib.ERR_UNAVAILABLE:

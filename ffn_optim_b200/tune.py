@@ -171,7 +171,7 @@ def main(argv=None):
     ap.add_argument("--up-candidates", nargs="+", default=["basic"])
     ap.add_argument("--down-candidates", nargs="+", default=list(DOWN_IMPLS))
     ap.add_argument("--tiles", nargs="+", default=None, help="kernel variants to search (default: automatic)")
-    ap.add_argument("--schedules", nargs="+", default=None, choices=("static", "dynamic"))
+    ap.add_argument("--schedules", nargs="+", default=None, choices=("static", "dynamic", "static_synced"))
     ap.add_argument("--block-num", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--repeats", type=int, default=20)

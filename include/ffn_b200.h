@@ -84,7 +84,8 @@ typedef enum {
   FFN_B200_KERNEL_OK = 0,
   FFN_B200_KERNEL_PIPE_TIMEOUT = 1, /* an on-chip pipeline wait ran past the wait limit */
   FFN_B200_KERNEL_DEP_TIMEOUT = 2,  /* a down tile waited too long for its hidden rows */
-  FFN_B200_KERNEL_SK_TIMEOUT = 3,   /* a Stream-K owner waited too long for a partial */
+  FFN_B200_KERNEL_SK_TIMEOUT = 3,   /* a Stream-K owner (or a hidden-slice reduction) waited too
+                                       long for a partial */
   FFN_B200_KERNEL_PEER_TIMEOUT = 4, /* a band owner waited too long for another GPU's partial */
   FFN_B200_KERNEL_CLAIM_RANGE = 5,  /* a tile claim fell outside this launch's range: the
                                        counters were not reset after an earlier error */
@@ -105,7 +106,11 @@ typedef struct {
                             6: swap 16 with 256-wide K stages, 7: swap 64 with 128-wide K stages,
                             8/9/10: hidden-resident row blocks with a 64/128/256-column Y
                             (down_impl full_load_a only), 11/12: swap 16 / swap 64 with fp8
-                            weights (weight_format FFN_B200_WEIGHTS_FP8_ROWS only)) */
+                            weights (weight_format FFN_B200_WEIGHTS_FP8_ROWS only), 13: hidden-
+                            slice decode, M <= 16: clusters of 8 CTAs each owning 128 hidden
+                            rows, no hidden tensor in global memory, Y reduced over the
+                            clusters (automatic for M <= 16 when the clusters share the hidden
+                            super-blocks evenly; plan.row_split = 8 is the cluster size)) */
   int32_t raster_group; /* tile rows per raster group (default: balances A and B bytes per wave) */
   int32_t l2_policy;    /* 1: no L2 eviction hints (default); 2: evict-last on the row operand and
                            evict-first on the column operand (measured: far more DRAM traffic);
@@ -113,8 +118,9 @@ typedef struct {
                            4: evict-last on the row operand only */
   int32_t schedule;     /* data-parallel tile order: 1 static (owner c takes tiles c, c+C, ...),
                            2 dynamic (after its first tile each owner claims the next tile of the
-                           raster from a device counter); 0 = dynamic for CTA-pair tiles,
-                           static otherwise */
+                           raster from a device counter), 3 static with bounded drift (an owner
+                           starts its tile of wave i once every owner has started wave i-1);
+                           0 = dynamic for CTA-pair tiles, static otherwise */
   int32_t weight_format; /* ffn_b200_weight_format of W1 and W2 */
 } ffn_b200_problem;
 
@@ -145,9 +151,9 @@ typedef struct {
                                hidden-row-block readiness counters */
   int64_t flag_words;       /* u32 Stream-K partial-ready flags: 2 x block_num */
   int64_t status_words;     /* i32 status words */
-  int32_t schedule;         /* resolved schedule: 1 static, 2 dynamic */
+  int32_t schedule;         /* resolved schedule: 1 static, 2 dynamic, 3 static with bounded drift */
   int32_t row_split;        /* row-block plans: CTAs (one cluster) sharing each row block's H
-                               chunks, 1, 2 or 4; 1 for the other plans */
+                               chunks, 1, 2, 4 or 8; 1 for the other plans */
 } ffn_b200_plan;
 
 /* Device buffers.  ld* are row pitches in elements; each must be a multiple of 8 and each

@@ -95,8 +95,8 @@ def test_swiglu_vs_oracle(shape, variant):
 
 def test_swiglu_rejections():
     x, w1, w2, _ = _inputs(256, 64, 128, 64, torch.bfloat16, 1)
-    with pytest.raises(NotApplicable):  # full_load_a keeps Y in TMEM: N <= 256
-        prepare_ffn(x.cuda(), w1.cuda(), torch.zeros(300, 128, dtype=torch.bfloat16).cuda(), activation="swiglu",
+    with pytest.raises(NotApplicable):  # full_load_a keeps Y in TMEM: N <= 512
+        prepare_ffn(x.cuda(), w1.cuda(), torch.zeros(600, 128, dtype=torch.bfloat16).cuda(), activation="swiglu",
                     down_impl="full_load_a")
     with pytest.raises(ValueError):  # W1 must hold 2H rows
         prepare_ffn(x.cuda(), w1[:128].cuda(), w2.cuda(), activation="swiglu")

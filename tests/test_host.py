@@ -95,7 +95,8 @@ def test_selection():
     with pytest.raises(DependencyUnavailable):
         Selection(down_impl="full_load_b").require_available()
     Selection(down_impl="full_load_a").require_available()
-    # full_load_a: hidden row block on chip, Y row block in TMEM -> N <= 256 (BASELINE cfg2 yes, cfg1 no)
+    # full_load_a: hidden row block on chip, Y row block in TMEM (256 columns, two halves above
+    # that) -> N <= 512 (BASELINE cfg2 and cfg1)
     cfg2 = problem_from_shapes([6993, 100], [1000, 100], [250, 1000])
     plan = make_plan(cfg2, Selection(down_impl="full_load_a"), sm_count=148)
     # 55 row blocks on 148 SMs: clusters of 2 CTAs split each block's 8 H chunks
@@ -106,9 +107,15 @@ def test_selection():
     assert small.block_num == 16 and small.kernel["row_split"] == 1
     many = make_plan(problem_from_shapes([512, 256], [1024, 256], [256, 1024]), Selection(down_impl="full_load_a"),
                      sm_count=148)
-    assert many.kernel["row_split"] == 4 and many.block_num == 16
+    assert many.kernel["row_split"] == 8 and many.block_num == 32
+    # cfg1: 4 row blocks x 2 Y halves = 8 units, clusters of 8 CTAs split the 16 H chunks
+    cfg1 = make_plan(problem_from_shapes([512, 512], [2048, 512], [512, 2048]), Selection(down_impl="full_load_a"),
+                     sm_count=148)
+    assert cfg1.kernel["variant"] == 9 and cfg1.kernel["row_split"] == 8 and cfg1.block_num == 64
+    assert make_plan(problem_from_shapes([512, 512], [2048, 512], [512, 2048]), Selection(down_impl="full_load_a"),
+                     63, sm_count=148).kernel["row_split"] == 4
     with pytest.raises(NotApplicable):
-        make_plan(problem_from_shapes([512, 512], [2048, 512], [512, 2048]), Selection(down_impl="full_load_a"),
+        make_plan(problem_from_shapes([512, 512], [2048, 512], [520, 2048]), Selection(down_impl="full_load_a"),
                   sm_count=148)
     with pytest.raises(ValueError):  # a two-phase tile cannot run full_load_a, nor the reverse
         make_plan(cfg2, Selection(down_impl="full_load_a"), sm_count=148, tile="cta128x256")
@@ -145,6 +152,22 @@ def _units(phase, C):
     return units
 
 
+def _check_hslice_cover(k, p):
+    """Hidden-slice plan: every 128-row hidden block is owned by exactly one CTA (super-block
+    sb -> cluster sb mod CL, CTA rank r -> block sb*8 + r), every 128-row n-block of Y by one
+    cluster rank, and the partials and counters fit the plan's buffers."""
+    S = k["row_split"]
+    CL = k["block_num"] // S
+    nhb, nnb = k["up"]["tiles_r"], k["down"]["tiles_r"]
+    assert S in (2, 4, 8) and k["block_num"] % S == 0 and p.m <= 16 and k["tile_n"] == 16
+    sb_n, nbr = -(-nhb // S), -(-nnb // S)
+    owned = sorted(sb * S + r for cl in range(CL) for sb in range(cl, sb_n, CL) for r in range(S))
+    assert owned == list(range(sb_n * S)) and CL <= sb_n
+    assert sorted(r * nbr + j for r in range(S) for j in range(nbr))[:nnb] == list(range(nnb))
+    assert k["workspace_floats"] == CL * S * nbr * 128 * 16 and k["counter_words"] == 6 + S
+    assert k["up"]["k_blocks"] == -(-p.k // 64) and k["down"]["k_blocks"] == -(-p.h // 64)
+
+
 @pytest.mark.parametrize("case_id", [c["case_id"] for c in C.load_cases()])
 @pytest.mark.parametrize("tile", [None, "pair256x256"])
 def test_plan_covers_every_k_block_once(case_id, tile):
@@ -159,6 +182,9 @@ def test_plan_covers_every_k_block_once(case_id, tile):
             assert down == "streamk"
             continue
         k = plan.kernel
+        if k["variant"] == 12:  # hidden-slice decode: clusters of 8 CTAs over hidden super-blocks
+            _check_hslice_cover(k, p)
+            continue
         assert k["block_num"] == 148
         owners_n = 148 // (2 if k["cta_pair"] else 1)
         if tile:
@@ -226,12 +252,32 @@ def test_dynamic_claims_cover_every_tile_once(dp, C):
 
 
 def test_baseline_variants():
-    want = {"cfg3_bf16": (1, 16), "cfg4_bf16": (0, 256), "cfg5_bf16": (0, 256), "cfg1_fp16": (0, 128),
-            "cfg2_bf16": (0, 128)}
-    for cid, (swap, bn) in want.items():
+    want = {"cfg3_bf16": (1, 16, 12), "cfg4_bf16": (0, 256, 0), "cfg5_bf16": (0, 256, 0), "cfg1_fp16": (0, 128, 1),
+            "cfg2_bf16": (0, 128, 1)}
+    for cid, (swap, bn, variant) in want.items():
         case = C.get_case(cid)
         plan = make_plan(C.case_problem(case), Selection(down_impl=case["down_impl"]), sm_count=148)
-        assert (plan.kernel["swap_ab"], plan.kernel["tile_n"]) == (swap, bn), cid
+        assert (plan.kernel["swap_ab"], plan.kernel["tile_n"], plan.kernel["variant"]) == (swap, bn, variant), cid
+    # cfg3 decode: 32 clusters of 4 CTAs (16 clusters of 8 do not fit one wave: a B200 holds
+    # 15), each CTA owning 128 of the 16384 hidden rows
+    case = C.get_case("cfg3_bf16")
+    k = make_plan(C.case_problem(case), Selection(down_impl="streamk"), sm_count=148).kernel
+    assert k["block_num"] == 128 and k["row_split"] == 4
+    # 8192 hidden rows: 8 clusters of 8; 40000: no single wave, the most even share (8: 40 / 45)
+    p8 = problem_from_shapes([16, 4096], [8192, 4096], [4096, 8192])
+    assert make_plan(p8, Selection(), sm_count=148).kernel["row_split"] == 8
+    p40 = problem_from_shapes([3, 136], [40000, 136], [200, 40000])
+    k40 = make_plan(p40, Selection(), sm_count=148, tile="hslice16").kernel
+    assert k40["row_split"] == 8 and k40["block_num"] == 120
+    # not for 17 tokens or a single super-block; forced where the swap16 tile applies
+    for m, h, gelu, tile, want_v in ((17, 16384, "rational", None, 3), (16, 1024, "rational", None, 2),
+                                     (5, 1000, "erf", "hslice16", 12), (1, 64, "rational", "hslice16", 12)):
+        p = problem_from_shapes([m, 4096], [h, 4096], [4096, h])
+        k = make_plan(p, Selection(down_impl="basic"), sm_count=148, gelu=gelu, tile=tile).kernel
+        assert k["variant"] == want_v, (m, h, gelu, tile)
+    with pytest.raises(ValueError):
+        make_plan(problem_from_shapes([17, 4096], [16384, 4096], [4096, 16384]), Selection(), sm_count=148,
+                  tile="hslice16")
 
 
 # ---------------------------------------------------------------- the C ABI
@@ -275,7 +321,7 @@ def test_c_planner_rejects_bad_problems(lib):
         assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_INVALID
     prob = _lib.Problem(64, 64, 64, 64, 1, 2, 0, 0, 148)  # full_load_b
     assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_UNAVAILABLE
-    prob = _lib.Problem(64, 64, 64, 300, 1, 1, 0, 0, 148)  # full_load_a with N > 256
+    prob = _lib.Problem(64, 64, 64, 600, 1, 1, 0, 0, 148)  # full_load_a with N > 512
     assert lib.ffn_b200_make_plan(ctypes.byref(prob), ctypes.byref(info)) == _lib.ERR_NOT_APPLICABLE
     # prepare without a usable device fails cleanly (no GPU in the CPU suite, or bad pointers)
     bufs = _lib.Buffers()
