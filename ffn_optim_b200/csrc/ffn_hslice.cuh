@@ -15,7 +15,7 @@
 //   partial: the fp32 [N/S x 16] partial of each cluster goes to global memory, and
 //   reduce:  Y rows of rank r are summed over the clusters (ascending cluster order) by the
 //            rank-r CTAs of all clusters, each taking an equal share of those rows (coalesced
-//            L2 loads, 16 clusters' partials in flight per thread).
+//            L2 loads, 32 clusters' partials in flight per thread).
 //
 // Every CTA streams 128 rows of W1 and 128 hidden columns' worth of W2 (S*128 columns for
 // N/S rows): equal bytes, one pass over HBM, and the only cross-cluster wait is the final
@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 4, 1) ffn_hslice_kernel(co
         if (ew == 0 && lane == 0) trace_mark(p, kTrDownReady);  // this CTA's partial released
         // Reduction of this rank's Y rows: every rank-r CTA of the CL clusters takes an equal
         // share [row0, row0 + nrows).  Work item (token quad q, row): the CL partial float4s
-        // (one per cluster; a warp's 32 rows are 512 contiguous bytes of each) are loaded 16 at
+        // (one per cluster; a warp's 32 rows are 512 contiguous bytes of each) are loaded 32 at
         // a time, then summed in ascending cluster order.
         const int rows_r = NBR * kBM;              // Y rows of rank r
         const int share = (rows_r + CL - 1) / CL;  // rows per rank-r CTA
@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * 4, 1) ffn_hslice_kernel(co
             const float4* src = base4 + static_cast<size_t>(q) * npad + n;  // cluster 0's float4
             const size_t cstride = 4 * npad;                                 // next cluster
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            constexpr int kBatch = 16;
+            constexpr int kBatch = 32;  // (32 clusters' float4s in flight per thread: one L2 round trip for cfg3)
 #pragma unroll 1
             for (int c0 = 0; c0 < CL; c0 += kBatch) {
               float4 t[kBatch];
