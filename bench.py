@@ -74,7 +74,7 @@ def parse():
     ap.add_argument("--weights", choices=("native", "fp8"), default="native",
                     help="fp8: e4m3 weights with per-row scales, widened on chip (decode tiles, M <= 64)")
     ap.add_argument("--schedule", choices=("static", "dynamic", "static_synced"), default=None,
-                    help="data-parallel tile order (default: dynamic for CTA-pair tiles, static otherwise; "
+                    help="data-parallel tile order (default: static_synced for CTA-pair tiles, static otherwise; "
                          "static_synced: static with each wave started after every owner started the previous one)")
     ap.add_argument("--raster-group", type=int, default=None,
                     help="N=1: tile rows per raster group (default: the planner's balanced choice)")
@@ -733,7 +733,7 @@ def main():
                 "config": {"workload": args.workload, "x": list(p.input_shape), "w1": [p.h, p.k], "w2": [p.n, p.h],
                            "down_impl": down, "parallelism": parallelism, "block_num": plan.block_num,
                            "kernel_variant": variant,
-                           "schedule": {1: "static", 2: "dynamic"}.get(plan.kernel.get("schedule")),
+                           "schedule": {1: "static", 2: "dynamic", 3: "static_synced"}.get(plan.kernel.get("schedule")),
                            "weights": args.weights,
                            "l2": "L2 flushed between steps (512 MB write)" if flush else "inputs larger than L2, no flush"},
                 "gpu_launches": launches * args.steps * world, "clocks": clocks, "roofline": roofline,

@@ -498,8 +498,13 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   } else if (pr->m <= 64) {
     variant = 3;
   } else {
+    // Long prefill runs (at least 8 waves of 256x256 tiles): CTA pairs, whose halved
+    // shared-memory traffic per FLOP and deeper ring run the tensor pipe busier at the same
+    // power (cfg4: 90 % vs 87 % tensor-pipe activity; cfg5: 1280 vs 1231 TFLOP/s on one box).
     const int64_t t256 = cdiv(pr->m, 128) * cdiv(pr->h, 256);
-    variant = t256 >= 2 * static_cast<int64_t>(grid) ? 0 : 1;
+    const int64_t p256 = cdiv(pr->m, 256) * cdiv(pr->h, 256);
+    if (grid >= 2 && (grid % 2) == 0 && p256 >= 8 * static_cast<int64_t>(grid / 2)) variant = 4;
+    else variant = t256 >= 2 * static_cast<int64_t>(grid) ? 0 : 1;
   }
   const Variant& v = kVariants[variant];
   const int ncta = v.pair ? 2 : 1;
@@ -514,7 +519,9 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   // wave pulls through L2.
   int group = pr->raster_group;
   if (group <= 0) {
-    const double balanced = std::sqrt(static_cast<double>(C) * v.bn / tile_m);
+    // (CTA pairs: half the balanced height -- measured on cfg5, 4 pair rows beat 8 by 1-4 %
+    // and 16 loses 6 %.)
+    const double balanced = std::sqrt(static_cast<double>(C) * v.bn / tile_m) / (v.pair ? 2.0 : 1.0);
     group = static_cast<int>(std::lround(balanced));
     // Prefer a nearby divisor of the tile-row count so no group is a ragged remainder
     // (measured on cfg5: 16 rows of 128 beat 17 by 2 %).
@@ -562,12 +569,13 @@ int ffn_b200_make_plan(const ffn_b200_problem* pr, ffn_b200_plan* out) {
   out->counter_words = ffnb200::kClaimWords + (v.swap ? out->up.tiles_q : out->up.tiles_r);
   out->flag_words = 2ll * C * ncta;
   out->status_words = 4;
-  // Automatic: dynamic claims for CTA-pair plans, whose pairs drift apart under the static
-  // order (cfg5: 773 us of spread at the phase change, 189 GB of DRAM reads against 93 GB
-  // dynamic); static for one-CTA tiles, whose cooperative launch keeps GPC-major placement
-  // and little drift (cfg5: 52 GB static against 64 GB dynamic) and for decode grids of one
-  // or two waves, where a claim would only add its latency.
-  out->schedule = pr->schedule ? pr->schedule : (v.pair ? 2 : 1);
+  // Automatic: the wave-synchronised static order for CTA-pair plans, whose pairs drift apart
+  // under the plain static order (cfg5: 773 us of spread at the phase change, 189 GB of DRAM
+  // reads) and lose their placement under dynamic claims (cfg5: 1253-1263 TFLOP/s dynamic,
+  // 1279-1283 synced); static for one-CTA tiles, whose cooperative launch keeps GPC-major
+  // placement and little drift (cfg5: 52 GB static against 64 GB dynamic) and for decode
+  // grids of one or two waves, where a claim would only add its latency.
+  out->schedule = pr->schedule ? pr->schedule : (v.pair ? 3 : 1);
   out->row_split = 1;
   // Decode (M <= 16): the hidden-slice kernel where its clusters share the work evenly.
   if (slice_forced || (pr->tile_variant == 0 && variant == 2)) {

@@ -101,7 +101,9 @@ typedef struct {
   int32_t block_num;   /* persistent CTA count; 0 = one per SM */
   int32_t sm_count;    /* SMs of the target device; 0 = query the current device */
   /* Tuning overrides, 0 = automatic (benchmarks and tests use them): */
-  int32_t tile_variant; /* 1 + variant id forces one kernel variant
+  int32_t tile_variant; /* 1 + variant id forces one kernel variant (automatic: CTA pairs for long
+                           prefill runs -- at least 8 waves of 256x256 tiles --, else 128x256 or
+                           128x128 one-CTA tiles; decode tiles for M <= 64)
                            (1: 128x256, 2: 128x128, 3: swap 16, 4: swap 64, 5: CTA pair 256x256,
                             6: swap 16 with 256-wide K stages, 7: swap 64 with 128-wide K stages,
                             8/9/10: hidden-resident row blocks with a 64/128/256-column Y
@@ -120,7 +122,7 @@ typedef struct {
                            2 dynamic (after its first tile each owner claims the next tile of the
                            raster from a device counter), 3 static with bounded drift (an owner
                            starts its tile of wave i once every owner has started wave i-1);
-                           0 = dynamic for CTA-pair tiles, static otherwise */
+                           0 = 3 for CTA-pair tiles, static otherwise */
   int32_t weight_format; /* ffn_b200_weight_format of W1 and W2 */
 } ffn_b200_problem;
 

@@ -252,12 +252,17 @@ def test_dynamic_claims_cover_every_tile_once(dp, C):
 
 
 def test_baseline_variants():
-    want = {"cfg3_bf16": (1, 16, 12), "cfg4_bf16": (0, 256, 0), "cfg5_bf16": (0, 256, 0), "cfg1_fp16": (0, 128, 1),
+    want = {"cfg3_bf16": (1, 16, 12), "cfg4_bf16": (0, 256, 4), "cfg5_bf16": (0, 256, 4), "cfg1_fp16": (0, 128, 1),
             "cfg2_bf16": (0, 128, 1)}
     for cid, (swap, bn, variant) in want.items():
         case = C.get_case(cid)
         plan = make_plan(C.case_problem(case), Selection(down_impl=case["down_impl"]), sm_count=148)
         assert (plan.kernel["swap_ab"], plan.kernel["tile_n"], plan.kernel["variant"]) == (swap, bn, variant), cid
+    # cfg5 prefill: CTA pairs, wave-synchronised static order, raster groups of 4 pair rows
+    k5 = make_plan(C.case_problem(C.get_case("cfg5_bf16")), Selection(), sm_count=148).kernel
+    assert k5["cta_pair"] == 1 and k5["schedule"] == 3 and k5["up"]["group"] == 4 and k5["tile_m"] == 256
+    # the reference's block_num=8 keeps one-CTA tiles for small runs, pairs for long ones
+    assert make_plan(C.case_problem(C.get_case("cfg1_fp16")), Selection(), 8, sm_count=148).kernel["cta_pair"] == 0
     # cfg3 decode: 32 clusters of 4 CTAs (16 clusters of 8 do not fit one wave: a B200 holds
     # 15), each CTA owning 128 of the 16384 hidden rows
     case = C.get_case("cfg3_bf16")
