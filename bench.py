@@ -112,14 +112,23 @@ def peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def traffic_for(workload):
-    """DRAM bytes per launch of the fused kernel from the committed ncu summary, if any."""
+def traffic_for(workload, variant):
+    """DRAM bytes per launch of the kernel variant that ran on this workload, from the
+    committed ncu summary ("<workload>/<variant>" keys), if any."""
     f = ROOT / "profiles" / "traffic.json"
     if f.exists():
         d = json.loads(f.read_text())
-        if workload in d:
-            return d[workload]
+        return d.get(f"{workload}/{variant}")
     return None
+
+
+def kernel_name(variant):
+    """The CUDA kernel a tile variant runs."""
+    if variant and variant.startswith("hslice"):
+        return "ffn_hslice_kernel"
+    if variant and variant.startswith("rowblock"):
+        return "ffn_rowblock_kernel"
+    return "ffn_fused_kernel"
 
 
 class ClockSampler:
@@ -617,14 +626,24 @@ def main():
             else runner.chunks[0].prepared if world > 1 else runner).plan
     variant = {v: k for k, v in _lib_variants().items()}.get(plan.kernel["variant"] + 1)
     per_launch_ms = ms_step / launches
-    achieved = fl / world / launches / (per_launch_ms / 1e3) / 1e12
-    roofline = {"bound": "tensor", "achieved": achieved, "peak": burst, "unit": "TFLOP/s", "frac": achieved / burst,
-                "traffic": traffic_for(args.workload) if world == 1 else None,
-                "traffic_source": "profiles/traffic.json (ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
-                                  "launch of this workload)" if world == 1 else None,
-                "peak_kind": f"{src} burst bf16 (MEASURED_PEAKS.json)" if src == "measured" else "fallback burst bf16",
-                "frac_of_sustained": achieved / sustained, "kernel": "ffn_fused_kernel",
-                "per_launch_us": per_launch_ms * 1e3}
+    # The launch's own work: one rank's share of the FLOPs, its M rows of X/Y plus the weights
+    # it streams (the bound is whichever roof is slower at the measured peaks).
+    ub_launch = unique_bytes(p, 1 if args.weights == "fp8" else 2) / world / launches
+    hbm_bound = ub_launch / (hbm * 1e9) > fl / world / launches / (burst * 1e12)
+    if hbm_bound:
+        achieved = ub_launch / (per_launch_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "peak_kind": f"{src} HBM copy (MEASURED_PEAKS.json)" if src == "measured" else "fallback HBM"}
+    else:
+        achieved = fl / world / launches / (per_launch_ms / 1e3) / 1e12
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": burst, "unit": "TFLOP/s", "frac": achieved / burst,
+                    "peak_kind": f"{src} burst bf16 (MEASURED_PEAKS.json)" if src == "measured" else "fallback burst bf16",
+                    "frac_of_sustained": achieved / sustained}
+    traffic = traffic_for(args.workload, variant) if world == 1 else None
+    roofline.update(traffic=traffic,
+                    traffic_source=("profiles/traffic.json (ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
+                                    f"launch of {args.workload} with {variant})") if traffic else None,
+                    kernel=kernel_name(variant), variant=variant, per_launch_us=per_launch_ms * 1e3)
 
     # ---- N = 1: end to end through the public API, CPU baseline with its parity check
     e2e = cpu = None
