@@ -217,3 +217,32 @@ def make_inputs(case, device="cpu"):
             return buf[..., ::2]
         x, w1, w2 = map(strided, (x, w1, w2))
     return x, w1, w2
+
+
+def reference_stream_inputs(case, device="cpu"):
+    """(x, w1, w2) drawn exactly as the reference draws its smoke-case inputs
+    (common/cases.py:34-50): one CPU ``torch.Generator`` seeded with the case's seed, standard
+    normal draws for X (the input shape), then W1 [H, K] scaled by K**-0.5, then W2 [N, H]
+    scaled by H**-0.5, each rounded to the case's dtype; ``noncontiguous`` cases get the same
+    stride-2 views.  The draws are sequential over whole tensors, so this form is for the
+    small smoke cases; the BASELINE configurations use :func:`make_inputs` (row-addressable
+    streams)."""
+    import torch
+
+    p = case_problem(case)
+    gen = torch.Generator(device="cpu").manual_seed(case.get("seed", 0))
+    dtype = getattr(torch, p.dtype)
+
+    def sample(shape, scale=1.0):
+        return (torch.randn(shape, generator=gen) * scale).to(dtype).to(device)
+
+    x = sample(p.input_shape)
+    w1 = sample((p.h, p.k), p.k ** -0.5)
+    w2 = sample((p.n, p.h), p.h ** -0.5)
+    if case.get("noncontiguous", False):
+        def strided(t):
+            buf = torch.empty((*t.shape[:-1], t.shape[-1] * 2), dtype=t.dtype, device=t.device)
+            buf[..., ::2].copy_(t)
+            return buf[..., ::2]
+        x, w1, w2 = map(strided, (x, w1, w2))
+    return x, w1, w2

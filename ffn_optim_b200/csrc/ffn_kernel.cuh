@@ -102,7 +102,7 @@ struct Params {
   // its band in ascending rank order.
   int rb_split;          // row-block kernel: CTAs (a cluster) sharing one row block's H chunks
   int kserp;             // 1: serpentine K order over the waves of data-parallel tiles (see the producer)
-  int wave_sync;         // 1 (static schedule): an owner starts wave i once every owner started wave i - 1
+  int wave_sync;         // static schedule: wave lag of the bounded-drift order (0 = off, 1 = schedule 3)
   int hs_superblocks;    // hidden-slice decode kernel: super-blocks of (cluster size) x 128 hidden rows
   int hs_nbr;            // hidden-slice decode kernel: 128-row blocks of Y per cluster rank
   int rs_world, rs_rank, rs_band_tiles;
@@ -1185,16 +1185,17 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
               break;
             }
             if (t >= s.dp) break;
-            if (p.wave_sync && !p.dyn) {
+            if (p.wave_sync > 0 && !p.dyn) {
               // Static order with bounded drift: start wave i = t / C only once every owner has
-              // started its tile of wave i - 1 (the phase's started-tile count, claims[ph],
-              // grows by exactly dp per launch), so owners that share operand strips stay
-              // within one tile of each other.
+              // started its tile of wave i - wave_sync (claims[ph] counts started tiles; it
+              // grows by exactly dp per launch).  (Lags of 2 and 4 waves measured 7 % and 10 %
+              // slower on cfg5 CTA pairs, and synchronising within tiles -- every 16 to 64
+              // k-steps -- 15-17 % slower: owners then wait on the slowest at every step.)
               if (!need_epoch()) { ok = false; break; }
               const long long wave = t / p.C;
-              if (wave > 0) {
-                const unsigned long long want =
-                    (epoch - 1ull) * static_cast<unsigned long long>(s.dp) + static_cast<unsigned long long>(wave * p.C);
+              if (wave >= p.wave_sync) {
+                const unsigned long long want = (epoch - 1ull) * static_cast<unsigned long long>(s.dp) +
+                                                static_cast<unsigned long long>((wave - p.wave_sync + 1) * p.C);
                 const uint64_t t0 = gtimer();
                 uint32_t n = 0;
 #pragma unroll 1

@@ -13,7 +13,10 @@ rows, the output bit patterns of
                           to the input dtype)
 
 together with sha256 digests of the inputs so a test can prove it regenerated the same
-inputs.  ``gelu.npz`` holds the reference's ``gelu_rational`` and torch's exact GELU on
+inputs.  For the reference's own smoke cases (``configs/v1_cases.json``) it also writes
+``ref_<case_id>.npz``: the inputs exactly as the reference's ``common/cases.py::make_inputs``
+draws them (its torch.Generator stream; bit patterns of the logical tensors) and the two
+outputs above for every row, so the kernel is checked on the reference's own tensors.  ``gelu.npz`` holds the reference's ``gelu_rational`` and torch's exact GELU on
 linspace(-10, 10, 10001).  Rows are independent in an FFN, so a row subset pins the
 whole computation for those rows.  The fixtures are produced once, here, and committed;
 the tests never import the reference.
@@ -93,6 +96,21 @@ def main():
                             golden=bits(gold), staged_rational=bits(staged), dtype=p.dtype,
                             torch_version=torch.__version__)
         print(case["case_id"], rows.shape, gold.shape)
+
+    # The reference's smoke cases, on the reference's own input stream.
+    from common.cases import load_cases as ref_load_cases, make_inputs as ref_make_inputs
+    for case in ref_load_cases(Path(args.reference).resolve() / "configs" / "v1_cases.json"):
+        if args.case and case["case_id"] not in args.case:
+            continue
+        x_t, w1_t, w2_t = ref_make_inputs(case)
+        with torch.no_grad():
+            gold = ffn_torch(x_t, w1_t, w2_t)
+            staged = ffn_torch(x_t, w1_t, w2_t, staged=True, rational=True)
+        bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        np.savez_compressed(HERE / f"ref_{case['case_id']}.npz", x=bits(x_t), w1=bits(w1_t), w2=bits(w2_t),
+                            golden=bits(gold), staged_rational=bits(staged), dtype=case["dtype"],
+                            torch_version=torch.__version__)
+        print("ref_" + case["case_id"], tuple(x_t.shape), tuple(gold.shape))
 
 
 if __name__ == "__main__":

@@ -72,6 +72,28 @@ def test_small_cases_vs_reference_golden(case_id, down_impl):
     assert_criterion(got, fx["golden"], dt)
 
 
+@pytest.mark.parametrize("case_id", ["aligned_fp16", "tails_bf16", "rank8_fp16"])
+@pytest.mark.parametrize("down_impl", ["basic", "streamk", "full_load_a"])
+def test_reference_smoke_cases_on_reference_inputs(case_id, down_impl):
+    """The reference's smoke cases on the tensors the reference itself draws
+    (common/cases.py:34-50, restated by ``cases.reference_stream_inputs`` and checked bit for
+    bit against the reference-generated fixture ``ref_<case>.npz``), views and all, against
+    the reference's ``ffn_torch`` outputs on the same tensors."""
+    fx = np.load(GOLDEN / f"ref_{case_id}.npz")
+    dt = str(fx["dtype"])
+    x, w1, w2 = C.reference_stream_inputs(C.get_case(case_id), device="cuda")
+    assert np.array_equal(bits_of(x.contiguous()).reshape(fx["x"].shape), fx["x"])
+    try:
+        prepared, y = run(x, w1, w2, down_impl=down_impl)
+    except NotApplicable:
+        assert down_impl == "streamk"
+        pytest.skip("Stream-K not applicable")
+    assert tuple(y.shape) == fx["golden"].shape and y.dtype == x.dtype
+    got = bits_of(y).reshape(-1, fx["golden"].shape[-1])
+    assert_close_bits(got, fx["staged_rational"].reshape(got.shape), dt)
+    assert_criterion(got, fx["golden"].reshape(got.shape), dt)
+
+
 @pytest.mark.parametrize("case_id", ["cfg1_fp16", "cfg2_bf16", "tails_bf16"])
 def test_erf_gelu_vs_reference_golden(case_id):
     case = C.get_case(case_id)

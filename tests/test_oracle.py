@@ -5,6 +5,7 @@ The fixtures in tests/golden/ were produced by the reference's validation/refere
 """
 import numpy as np
 import pytest
+import torch
 
 from ffn_optim_b200 import cases as C
 from oracle import ffn_oracle as O
@@ -82,6 +83,30 @@ def test_oracle_matches_reference_golden(case_id):
 def test_oracle_matches_reference_golden_large(case_id):
     fx, dt, x, a, b = _oracle_rows(case_id)
     assert_pinned(O.ffn(x, a, b, dt), fx["golden"], dt)
+
+
+REF_SMOKE = ["aligned_fp16", "tails_bf16", "rank8_fp16"]
+
+
+@pytest.mark.parametrize("case_id", REF_SMOKE)
+def test_reference_stream_inputs_and_oracle(case_id):
+    """The reference's smoke cases on the reference's own input stream: the restated
+    generator (``cases.reference_stream_inputs``) reproduces the tensors the reference's
+    ``common/cases.py::make_inputs`` drew (fixture ``ref_<case>.npz``) bit for bit, and the
+    oracle on them matches the reference's ``ffn_torch`` outputs."""
+    fx = np.load(GOLDEN / f"ref_{case_id}.npz")
+    dt = str(fx["dtype"])
+    x, w1, w2 = C.reference_stream_inputs(C.get_case(case_id))
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    for t, name in ((x, "x"), (w1, "w1"), (w2, "w2")):
+        assert np.array_equal(bits(t), fx[name]), name
+    f = lambda b: O.from_bits(b, dt)  # noqa: E731
+    xs = f(fx["x"]).reshape(-1, fx["x"].shape[-1])
+    ours = O.ffn(xs, f(fx["w1"]), f(fx["w2"]), dt)
+    gold = fx["golden"].reshape(-1, fx["golden"].shape[-1])
+    assert_pinned(ours, gold, dt, identical=0.95)
+    staged = O.ffn(xs, f(fx["w1"]), f(fx["w2"]), dt, staged=True, rational=True)
+    assert_pinned(staged, fx["staged_rational"].reshape(gold.shape), dt, 0.95, 1e-4)
 
 
 def test_seeded_inputs_are_deterministic():
