@@ -950,10 +950,6 @@ int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, int32_t
   P.rs_rank = rank;
   P.rs_band_tiles = pl.down.tiles_r / world;
   P.rs_fp32 = partial == FFN_B200_PARTIAL_F32 ? 1 : 0;
-  // Interleave the phases by raster group (static, data-parallel plans): the pushes of the
-  // down tiles then spread over the whole launch rather than its second half (cfg5 at 8 GPUs
-  // moves 1.88 GB of fp32 partials per GPU per launch over NVLink).
-  P.interleave = (pl.schedule == 1 && pl.up.sk_tiles == 0 && pl.down.sk_tiles == 0) ? 1 : 0;
   const int64_t stage_rows = 2ll * world * (pl.down.tiles_r / world) * pl.down.tiles_q * ffnb200::kBM;
   for (int r = 0; r < world; ++r) {
     P.rs_stage[r] = stage_ptrs[r];

@@ -103,7 +103,6 @@ struct Params {
   int rb_split;          // row-block kernel: CTAs (a cluster) sharing one row block's H chunks
   int kserp;             // 1: serpentine K order over the waves of data-parallel tiles (see the producer)
   int wave_sync;         // static schedule: wave lag of the bounded-drift order (0 = off, 1 = schedule 3)
-  int interleave;        // 1: one static work list interleaving the phases by raster group (see the producer)
   int hs_superblocks;    // hidden-slice decode kernel: super-blocks of (cluster size) x 128 hidden rows
   int hs_nbr;            // hidden-slice decode kernel: 128-row blocks of Y per cluster rank
   int rs_world, rs_rank, rs_band_tiles;
@@ -717,9 +716,7 @@ __device__ __forceinline__ void tile_coords(const PhaseSched& s, int t, int& tr,
 __device__ __forceinline__ void unit_coords(const Params& p, const Unit& u, int& tr, int& tq) {
   const PhaseSched& s = u.phase ? p.dn : p.up;
   tile_coords(s, u.tile, tr, tq);
-  // (interleaved phases: the up tiles follow the same row order, so a raster group's down
-  // tiles find their hidden rows computed by the up group just before)
-  if ((u.phase == 1 || p.interleave) && p.rs_world > 1) tr = (tr + (p.rs_rank + 1) * p.rs_band_tiles) % s.tiles_r;
+  if (u.phase == 1 && p.rs_world > 1) tr = (tr + (p.rs_rank + 1) * p.rs_band_tiles) % s.tiles_r;
 }
 
 // Data-parallel tile t of a phase: the whole K range in one unit.
@@ -1158,46 +1155,8 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
           ++seq;
           return true;
         };
-        if (p.interleave) {
-          // Interleaved phases (static order, data-parallel tiles only): the raster groups of
-          // both phases form one sequence U0 U1 D0 U2 D1 ... U(G-1) D(G-2) D(G-1), where Ug /
-          // Dg are the up / down tiles of tile-row group g, and owner c takes entries c, c + C,
-          // ... of it.  A group's down tiles run one up group after its hidden rows, so the
-          // down work (and, under the fused reduce-scatter, its NVLink pushes) spreads over
-          // the whole launch instead of a second half.
-          const int G = (p.up.tiles_r + p.up.group - 1) / p.up.group;
-          auto seg_of = [&](int k, int& ph, int& g) {
-            if (k == 0) { ph = 0; g = 0; }
-            else if (k == 2 * G - 1) { ph = 1; g = G - 1; }
-            else if (k & 1) { ph = 0; g = (k + 1) / 2; }
-            else { ph = 1; g = k / 2 - 1; }
-          };
-          auto seg_len = [&](int ph, int g) {
-            const PhaseSched& s = ph ? p.dn : p.up;
-            return min(s.group, s.tiles_r - g * s.group) * s.tiles_q;
-          };
-          long long seg_start = 0;  // global index of segment k's first entry
-          int k = 0, sph = 0, sg = 0;
-          seg_of(0, sph, sg);
 #pragma unroll 1
-          for (long long idx = cta; ok && k < 2 * G; idx += p.C) {
-            while (k < 2 * G && idx >= seg_start + seg_len(sph, sg)) {
-              seg_start += seg_len(sph, sg);
-              if (++k < 2 * G) seg_of(k, sph, sg);
-            }
-            if (k >= 2 * G) break;
-            const PhaseSched& s = sph ? p.dn : p.up;
-            const int t = sg * s.group * s.tiles_q + static_cast<int>(idx - seg_start);
-            Unit u;
-            dp_unit(s, sph, t, u);
-            u.rev = p.kserp && ((idx / p.C) & 1) ? 1 : 0;
-            int w[8];
-            pack_unit(u, w);
-            if (!publish(w) || !do_loads(u)) ok = false;
-          }
-        }
-#pragma unroll 1
-        for (int ph = 0; ph < 2 && ok && !p.interleave; ++ph) {
+        for (int ph = 0; ph < 2 && ok; ++ph) {
           const PhaseSched& s = ph ? p.dn : p.up;
           // Data-parallel tiles.  Owner c's first tile is tile c; under the dynamic schedule
           // every later one is claimed (tile C + claim index) so that the tiles in flight
