@@ -17,7 +17,8 @@ Keys: ``value`` = useful TFLOP/s (2*M*(K*H + H*N) per step, whole job) with inpu
 in HBM.  N = 1: one fused kernel per step.  N > 1 (``--shard``, default ``hf``): H-sharded
 tensor parallelism with the reduce-scatter fused into the kernel (partial tiles pushed over
 NVLink as fp32); ``variants`` holds the same step timed with the M-sharded (no
-communication), NCCL reduce-scatter and input-dtype-partial variants.  ``e2e`` = the same
+communication), NCCL reduce-scatter, 24-bit-partial and input-dtype-partial variants,
+and (N >= 4) the fused reduce-scatter inside pairs of GPUs with M split over the pairs.  ``e2e`` = the same
 metric through the public API with X copied from pinned host memory and Y read back every
 step (N = 1: ``PreparedFFN.run_host``; N > 1: ``RowShardedFFN.run_host`` on every rank, the
 partitioning that moves each host byte over PCIe once).  ``roofline`` = the fused kernel
@@ -468,15 +469,24 @@ def make_runner(kind, x, w1, w2, down, args, world):
                         raster_group=args.raster_group,
                         weight_format=None if args.weights == "native" else args.weights)
         return r, r.run, 1, "single", (lambda g: g), r.run
-    if kind in ("hf", "hf_input"):
+    if kind in ("hf", "hf_fp24", "hf_input"):
         from ffn_optim_b200.sharded import FusedTensorParallelFFN
 
-        partial = "fp32" if kind == "hf" else "input"
+        partial = {"hf": "fp32", "hf_fp24": "fp24", "hf_input": "input"}[kind]
         r = FusedTensorParallelFFN(x, w1, w2, down_impl=down, partial=partial)
         lo = r.local_rows()[0]
         per = len(r.local_rows())
         owned = lambda g: g - lo if lo <= g < lo + per else None  # noqa: E731
         label = f"tp-h{world} (reduce-scatter fused in the kernel, NVLink peer stores, {partial} partials)"
+        return r, r.run, 1, label, owned, r.run
+    if kind == "hf_tp2":
+        from ffn_optim_b200.sharded import TpDpFusedFFN
+
+        r = TpDpFusedFFN(x, w1, w2, tp=2, down_impl=down)
+        lo = r.lo_rows
+        per = r.hi_rows - r.lo_rows
+        owned = lambda g: g - lo if lo <= g < lo + per else None  # noqa: E731
+        label = f"tp2 x dp{world // 2} (fused reduce-scatter inside each pair of GPUs, fp32 partials; M split over the pairs)"
         return r, r.run, 1, label, owned, r.run
     if kind == "h":
         from ffn_optim_b200.sharded import TensorParallelFFN
@@ -688,7 +698,8 @@ def main():
         close_runner(runner)
         del runner, step, output
         torch.cuda.empty_cache()
-        for kind in [k for k in ("m", "h", "hf_input", "hf") if k != primary]:
+        kinds = ("m", "h", "hf_input", "hf_fp24") + (("hf_tp2",) if world >= 4 and world % 2 == 0 else ()) + ("hf",)
+        for kind in [k for k in kinds if k != primary]:
             r, st, nl, label, own, outp = make_runner(kind, x, w1, w2, down, args, world)
             for _ in range(args.warmup):
                 st()

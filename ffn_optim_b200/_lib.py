@@ -33,7 +33,7 @@ TILE_VARIANTS = {"cta128x256": 1, "cta128x128": 2, "swap16": 3, "swap64": 4, "pa
                  "swap16fp8": 11, "swap64fp8": 12, "hslice16": 13}
 WEIGHT_FORMATS = {"native": 0, "fp8": 1}
 # Element type of the partial tiles the fused reduce-scatter sends between GPUs.
-PARTIAL_TYPES = {"fp32": 0, "input": 1}
+PARTIAL_TYPES = {"fp32": 0, "input": 1, "fp24": 2}
 L2_POLICIES = {"none": 1, "stream_b": 2, "normal": 3, "keep_a": 4}
 SCHEDULES = {"static": 1, "dynamic": 2, "static_synced": 3}
 KERNEL_ERRORS = {0: "ok", 1: "on-chip pipeline wait timed out", 2: "hidden row-block readiness wait timed out",

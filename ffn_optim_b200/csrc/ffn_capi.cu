@@ -920,11 +920,12 @@ int ffn_b200_peer_free(void* dev_ptr) {
 int ffn_b200_reduce_scatter_bytes(const ffn_b200_handle* h, int world, int32_t partial, uint64_t* stage_bytes,
                                   uint64_t* flag_bytes) {
   if (!h || !stage_bytes || !flag_bytes || world < 2 || world > ffnb200::kMaxRanks) return FFN_B200_ERR_INVALID;
-  if (partial != FFN_B200_PARTIAL_F32 && partial != FFN_B200_PARTIAL_INPUT) return FFN_B200_ERR_INVALID;
+  if (partial != FFN_B200_PARTIAL_F32 && partial != FFN_B200_PARTIAL_INPUT && partial != FFN_B200_PARTIAL_F24)
+    return FFN_B200_ERR_INVALID;
   const ffn_b200_plan& pl = h->plan;
   if (pl.swap_ab || pl.cta_pair || pl.down.tiles_r % world) return FFN_B200_ERR_INVALID;
   const uint64_t band = static_cast<uint64_t>(pl.down.tiles_r / world) * pl.down.tiles_q;
-  const uint64_t esize = partial == FFN_B200_PARTIAL_F32 ? 4 : 2;
+  const uint64_t esize = partial == FFN_B200_PARTIAL_F32 ? 4 : (partial == FFN_B200_PARTIAL_F24 ? 3 : 2);
   *stage_bytes = 2ull * world * band * ffnb200::kBM * pl.tile_n * esize;
   *flag_bytes = 4ull * world * band;
   return FFN_B200_OK;
@@ -935,7 +936,8 @@ int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, int32_t
   if (!h || world < 2 || world > ffnb200::kMaxRanks || rank < 0 || rank >= world || !stage_ptrs || !flag_ptrs ||
       !y_local)
     return FFN_B200_ERR_INVALID;
-  if (partial != FFN_B200_PARTIAL_F32 && partial != FFN_B200_PARTIAL_INPUT) return FFN_B200_ERR_INVALID;
+  if (partial != FFN_B200_PARTIAL_F32 && partial != FFN_B200_PARTIAL_INPUT && partial != FFN_B200_PARTIAL_F24)
+    return FFN_B200_ERR_INVALID;
   const ffn_b200_plan& pl = h->plan;
   if (pl.swap_ab || pl.cta_pair || pl.down.tiles_r % world) return FFN_B200_ERR_INVALID;
   if (h->prob.m % (static_cast<int64_t>(world) * pl.tile_m) != 0) return FFN_B200_ERR_INVALID;
@@ -949,16 +951,20 @@ int ffn_b200_set_reduce_scatter(ffn_b200_handle* h, int world, int rank, int32_t
   P.rs_world = world;
   P.rs_rank = rank;
   P.rs_band_tiles = pl.down.tiles_r / world;
-  P.rs_fp32 = partial == FFN_B200_PARTIAL_F32 ? 1 : 0;
+  P.rs_format = partial == FFN_B200_PARTIAL_F32 ? 1 : (partial == FFN_B200_PARTIAL_F24 ? 2 : 0);
   const int64_t stage_rows = 2ll * world * (pl.down.tiles_r / world) * pl.down.tiles_q * ffnb200::kBM;
+  P.rs_lo_off = stage_rows * pl.tile_n * 2;  // format 2: the byte plane follows the 16-bit plane
   for (int r = 0; r < world; ++r) {
     P.rs_stage[r] = stage_ptrs[r];
     P.rs_flags[r] = static_cast<unsigned*>(flag_ptrs[r]);
-    // Bulk-store map over rank r's staging buffer ([rows][tile_n], no multicast).
-    const int e = P.rs_fp32 ? encode_2d_f32(&P.tm_rs[r], stage_ptrs[r], pl.tile_n, stage_rows, pl.tile_n,
-                                            ffnb200::kStoreRows)
-                            : encode_2d(&P.tm_rs[r], stage_ptrs[r], h->prob.dtype, pl.tile_n, stage_rows, pl.tile_n,
-                                        64, ffnb200::kStoreRows);
+    // Bulk-store maps over rank r's staging buffer ([rows][tile_n], no multicast).
+    int e = P.rs_format == 1 ? encode_2d_f32(&P.tm_rs[r], stage_ptrs[r], pl.tile_n, stage_rows, pl.tile_n,
+                                             ffnb200::kStoreRows)
+                             : encode_2d(&P.tm_rs[r], stage_ptrs[r], h->prob.dtype, pl.tile_n, stage_rows, pl.tile_n,
+                                         64, ffnb200::kStoreRows);
+    if (!e && P.rs_format == 2)  // the byte plane: 64-byte rows of a 64-column chunk
+      e = encode_2d_u8(&P.tm_rs_lo[r], static_cast<const uint8_t*>(stage_ptrs[r]) + P.rs_lo_off, pl.tile_n,
+                       stage_rows, pl.tile_n, 64, ffnb200::kStoreRows);
     if (e) return e;
   }
   return FFN_B200_OK;

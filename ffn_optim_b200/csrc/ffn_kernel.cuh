@@ -97,19 +97,21 @@ struct Params {
   const uint16_t* bias2;       // the hidden sums before the activation / to Y before rounding
   // Fused reduce-scatter of the down phase across `rs_world` GPUs (tensor parallel over H):
   // rank b owns the Y rows of tile rows [b*rs_band_tiles, (b+1)*rs_band_tiles).  A down tile
-  // of another rank's band is pushed as a partial (fp32, or rounded to the input dtype when
-  // rs_fp32 = 0) into that rank's staging buffer over NVLink; an owner sums the partials of
-  // its band in ascending rank order.
+  // of another rank's band is pushed as a partial (rs_format: 1 fp32; 2 fp32 rounded to 24
+  // bits; 0 rounded to the input dtype) into that rank's staging buffer over NVLink; an
+  // owner sums the partials of its band in ascending rank order.
   int rb_split;          // row-block kernel: CTAs (a cluster) sharing one row block's H chunks
   int kserp;             // 1: serpentine K order over the waves of data-parallel tiles (see the producer)
   int wave_sync;         // static schedule: wave lag of the bounded-drift order (0 = off, 1 = schedule 3)
   int hs_superblocks;    // hidden-slice decode kernel: super-blocks of (cluster size) x 128 hidden rows
   int hs_nbr;            // hidden-slice decode kernel: 128-row blocks of Y per cluster rank
   int rs_world, rs_rank, rs_band_tiles;
-  int rs_fp32;                     // 1: staged partials are fp32; 0: the input dtype
+  int rs_format;                   // staged partials: 0 input dtype, 1 fp32, 2 fp32 rounded to 24 bits
+  long long rs_lo_off;             // format 2: byte offset of the low-byte plane in a staging buffer
   void* rs_stage[kMaxRanks];       // per rank: [2 parity][world][band tiles][kBM][BN] partials
   unsigned* rs_flags[kMaxRanks];   // per rank: [world][band tiles] push counts (4 per launch)
   CUtensorMap tm_rs[kMaxRanks];    // store maps over each rank's staging, viewed as [rows][BN]
+  CUtensorMap tm_rs_lo[kMaxRanks]; // format 2: store maps over the low-byte planes ([rows][BN] bytes)
 };
 
 static_assert(sizeof(Params) <= 4096, "kernel parameters must fit the 4 KB parameter space");
@@ -1673,7 +1675,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
                 if (src == p.rs_rank) {
 #pragma unroll
                   for (int j = 0; j < 16; ++j) acc[j] = src == 0 ? v[16 * q + j] : acc[j] + v[16 * q + j];
-                } else if (p.rs_fp32) {
+                } else if (p.rs_format == 1) {
                   const float4* sp = reinterpret_cast<const float4*>(static_cast<const float*>(p.rs_stage[p.rs_rank]) +
                                                                      rs_row(src) + ch * 64 + 16 * q);
                   float4 w[4];
@@ -1685,6 +1687,29 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
                     acc[4 * j + 1] = src == 0 ? w[j].y : acc[4 * j + 1] + w[j].y;
                     acc[4 * j + 2] = src == 0 ? w[j].z : acc[4 * j + 2] + w[j].z;
                     acc[4 * j + 3] = src == 0 ? w[j].w : acc[4 * j + 3] + w[j].w;
+                  }
+                } else if (p.rs_format == 2) {
+                  // 24-bit partial: the high 16 bits of the rounded fp32 word from the u16
+                  // plane, the next 8 from the byte plane (low 8 bits zero).
+                  const size_t e0 = rs_row(src) + ch * 64 + 16 * q;
+                  const uint4* hp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.rs_stage[p.rs_rank]) + e0);
+                  const uint4 lw = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.rs_stage[p.rs_rank]) +
+                                                                         p.rs_lo_off + e0));
+                  const uint32_t lv[4] = {lw.x, lw.y, lw.z, lw.w};
+#pragma unroll
+                  for (int j = 0; j < 2; ++j) {
+                    const uint4 w = __ldcg(hp + j);
+                    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                      const int c = 8 * j + 2 * e;  // column of the low element of this pair
+                      const uint32_t b0 = (lv[c >> 2] >> (8 * (c & 3))) & 0xFFu;
+                      const uint32_t b1 = (lv[(c + 1) >> 2] >> (8 * ((c + 1) & 3))) & 0xFFu;
+                      const float lo = __uint_as_float((wv[e] << 16) | (b0 << 8));
+                      const float hi = __uint_as_float((wv[e] & 0xFFFF0000u) | (b1 << 8));
+                      acc[c] = src == 0 ? lo : acc[c] + lo;
+                      acc[c + 1] = src == 0 ? hi : acc[c + 1] + hi;
+                    }
                   }
                 } else {
                   const uint4* sp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.rs_stage[p.rs_rank]) +
@@ -1708,7 +1733,59 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
             // (the band owner adds the bias once, to the sum of all ranks' partials)
             if (p.bias2) add_bias<BF16, 64>(v, p.bias2, tq * BN + ch * 64, p.N);
           }
-          if (rs_push && p.rs_fp32) {
+          if (rs_push && p.rs_format == 2) {
+            // 24-bit partial for the owning GPU: each fp32 word rounded to nearest (ties to
+            // even) at bit 8, its high 16 bits sent as a u16 tile and the next 8 as a byte
+            // tile (two bulk stores per chunk and warp; 3/4 of the fp32 bytes over NVLink).
+            const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
+            const int srow = static_cast<int>(((static_cast<size_t>(epoch & 1u) * p.rs_world + p.rs_rank) * band +
+                                               rs_tile) * kBM) + sub * 32;
+            uint32_t hi2[32], lo4[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) lo4[j] = 0u;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              const uint32_t b = __float_as_uint(v[j]);
+              const uint32_t r24 = b + 0x7Fu + ((b >> 8) & 1u);
+              const uint32_t h16 = r24 >> 16;
+              if (j & 1) hi2[j >> 1] |= h16 << 16;
+              else hi2[j >> 1] = h16;
+              lo4[j >> 2] |= ((r24 >> 8) & 0xFFu) << (8 * (j & 3));
+            }
+#pragma unroll
+            for (int pl = 0; pl < 2; ++pl) {
+              const uint32_t sb = sE + static_cast<uint32_t>((ew * 2 + sbuf) * kStageBufBytes);
+              if (lane == 0) bulk_wait_read1();
+              __syncwarp();
+              if (pl == 0) {  // 32 rows x 128 B, 128B-swizzled
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const uint32_t addr = sb + lane * 128 + ((j ^ (lane & 7)) << 4);
+                  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(hi2[4 * j]),
+                               "r"(hi2[4 * j + 1]), "r"(hi2[4 * j + 2]), "r"(hi2[4 * j + 3])
+                               : "memory");
+                }
+              } else {  // 32 rows x 64 B, 64B-swizzled: 16-byte chunk c of row r at c ^ ((r >> 1) & 3)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t addr = sb + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4);
+                  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(lo4[4 * j]),
+                               "r"(lo4[4 * j + 1]), "r"(lo4[4 * j + 2]), "r"(lo4[4 * j + 3])
+                               : "memory");
+                }
+              }
+              fence_async_shared();
+              __syncwarp();
+              if (lane == 0) {
+                if (pl == 0) tma_store_2d(&p.tm_rs[rs_owner], sb, ch * 64, srow);
+                else tma_store_2d(&p.tm_rs_lo[rs_owner], sb, ch * 32, srow);  // (byte pairs: x in units of 2 bytes)
+                bulk_commit();
+              }
+              sbuf ^= 1;
+            }
+            continue;
+          }
+          if (rs_push && p.rs_format == 1) {
             // fp32 partial for the owning GPU: two 32-column halves (128-byte rows), each
             // staged 128B-swizzled in one of this warp's buffers and sent as one 4 KB bulk
             // store over NVLink, so the owner's sum sees the unrounded partial.

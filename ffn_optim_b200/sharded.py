@@ -223,8 +223,10 @@ class FusedTensorParallelFFN:
     staging buffer (peer bulk stores, then a system-scope release), and each rank sums the P
     partials of its own band in ascending rank order and stores its Y rows.  ``partial``
     selects what crosses NVLink: ``'fp32'`` (default; the owner sums unrounded partials, so
-    every output keeps the single-GPU error bound) or ``'input'`` (partials rounded to the
-    input dtype: half the NVLink bytes, up to P-1 extra roundings per output).  Staging and
+    every output keeps the single-GPU error bound), ``'fp24'`` (fp32 rounded to nearest at
+    24 bits -- sign, exponent, 15 mantissa bits -- sent as a 16-bit and an 8-bit plane: 3/4
+    of the fp32 bytes, a relative error below 2^-16 per partial) or ``'input'`` (partials
+    rounded to the input dtype: half the NVLink bytes, up to P-1 extra roundings per output).  Staging and
     push-count buffers are CUDA IPC buffers exchanged once at construction.  :meth:`run`
     launches one kernel and returns this rank's rows ``local_rows()`` of Y.
 
@@ -358,3 +360,73 @@ class FusedTensorParallelFFN:
 
             warnings.warn("FusedTensorParallelFFN dropped without close(): peer-visible buffers are leaked",
                           ResourceWarning, stacklevel=2)
+
+
+def tp_dp_groups(world: int, tp: int):
+    """Rank lists of the tensor-parallel groups of a ``tp`` x ``world/tp`` layout: ranks
+    [g*tp, (g+1)*tp) form group g (neighbouring ranks, so a group's peers share the node's
+    NVSwitch like any others).  Raises ValueError unless 2 <= tp <= world and tp divides world."""
+    if tp < 2 or tp > world or world % tp:
+        raise ValueError(f"tp must divide the world size ({world}) and be at least 2")
+    return [list(range(g * tp, (g + 1) * tp)) for g in range(world // tp)]
+
+
+def tp_dp_rows(m: int, world: int, tp: int, rank: int):
+    """Global Y rows [lo, hi) that ``rank`` owns in the tp x dp layout: its group's M slice
+    (``m_slices(m, world/tp)``), then the fused reduce-scatter's band of that slice for the
+    rank's position in the group (the slice must divide into tp equal bands)."""
+    groups = tp_dp_groups(world, tp)
+    g = rank // tp
+    lo, hi = m_slices(m, len(groups))[g]
+    if (hi - lo) % tp:
+        raise ValueError("each group's M slice must divide into tp equal bands")
+    per = (hi - lo) // tp
+    pos = rank - g * tp
+    return lo + pos * per, lo + (pos + 1) * per
+
+
+class TpDpFusedFFN:
+    """Two-level layout on one node: groups of ``tp`` GPUs each run the H-sharded FFN with
+    the fused reduce-scatter (:class:`FusedTensorParallelFFN`, fp32 partials by default) on
+    one M slice (``m_slices(M, world/tp)``); no communication between groups.  Each GPU
+    sends (tp-1)/tp of its slice's partial Y instead of (P-1)/P of the whole batch's, so the
+    NVLink bytes per GPU fall by about world/tp.  ``run`` returns this rank's rows
+    ``local_rows()`` (global indices, ``tp_dp_rows``).
+
+    Construction and :meth:`close` are collective over the whole world (every rank creates
+    every group's communicator, in the same order)."""
+
+    def __init__(self, x, w1, w2, *, tp=2, down_impl="basic", block_num=None, gelu="rational",
+                 tile="cta128x256", partial="fp32"):
+        import torch.distributed as dist
+
+        world, rank = dist.get_world_size(), dist.get_rank()
+        groups = tp_dp_groups(world, tp)
+        self.groups = [dist.new_group(ranks) for ranks in groups]
+        g = rank // tp
+        k = x.shape[-1]
+        m = x.numel() // k
+        self.lo_rows, self.hi_rows = tp_dp_rows(m, world, tp, rank)
+        lo, hi = m_slices(m, len(groups))[g]
+        self.inner = FusedTensorParallelFFN(x.reshape(m, k)[lo:hi], w1, w2, group=self.groups[g],
+                                            down_impl=down_impl, block_num=block_num, gelu=gelu, tile=tile,
+                                            partial=partial)
+        self.prepared = self.inner.prepared
+
+    def launches_per_run(self):
+        return 1
+
+    def run(self):
+        return self.inner.run()
+
+    def local_rows(self):
+        return list(range(self.lo_rows, self.hi_rows))
+
+    def check(self):
+        self.inner.check()
+
+    def close(self):
+        import torch.distributed as dist
+
+        self.inner.close()
+        dist.barrier()

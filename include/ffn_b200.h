@@ -230,9 +230,12 @@ FFN_B200_EXPORT int ffn_b200_peer_free(void* dev_ptr);
 
 /* Element type of the partial Y tiles that the fused reduce-scatter sends between GPUs:
  * fp32 (default: the owner sums unrounded partials, so P GPUs keep the single-GPU error
- * bound) or the input dtype (half the NVLink bytes; each partial is rounded once before the
- * sum, which adds up to P-1 roundings to every output). */
-typedef enum { FFN_B200_PARTIAL_F32 = 0, FFN_B200_PARTIAL_INPUT = 1 } ffn_b200_partial;
+ * bound), the input dtype (half the NVLink bytes; each partial is rounded once before the
+ * sum, which adds up to P-1 roundings to every output), or fp32 rounded to nearest at 24
+ * bits (sign, exponent, 15 mantissa bits: 3/4 of the fp32 bytes, sent as a 16-bit and an
+ * 8-bit plane; each partial carries a relative error below 2^-16, 128 times finer than a
+ * bf16 output ulp). */
+typedef enum { FFN_B200_PARTIAL_F32 = 0, FFN_B200_PARTIAL_INPUT = 1, FFN_B200_PARTIAL_F24 = 2 } ffn_b200_partial;
 
 /* Sizes of one rank's staging buffer (partial tiles of type `partial`, two launch
  * parities) and push counts for a `world`-GPU reduce-scatter of this handle's down phase. */

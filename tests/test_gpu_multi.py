@@ -2,13 +2,15 @@
 
 At world size 2 and at every GPU of the box (``torch.cuda.device_count()``), one process per
 GPU over NCCL: H-sharded tensor parallelism with the reduce-scatter fused into the kernel
-(fp32 partials, the default, and input-dtype partials), H-sharded with an NCCL
-reduce-scatter, and M-sharded.  Every rank's output rows are checked against the oracle
+(fp32 partials, the default; fp32 rounded to 24 bits; input-dtype partials), H-sharded with an NCCL
+reduce-scatter, M-sharded, and (4 GPUs or more) pairs of GPUs running the fused
+reduce-scatter on M slices.  Every rank's output rows are checked against the oracle
 (``oracle/ffn_oracle.py``, the numpy restatement of the reference's ``ffn_torch``) on the
 same inputs: the reference criterion with the max-abs bound (``compare(strict=True)``)
 against the exact-erf golden for every variant, and the single-GPU bound -- two output ulps
 + 1e-3*max|golden| against the golden of the kernel's arithmetic (rational GELU, staged
-hidden) -- for the variants that sum unrounded partials (fp32 reduce-scatter, M-shard).
+hidden) -- for the variants that sum unrounded or 24-bit partials (fp32 and fp24
+reduce-scatter, M-shard).
 The variants that round each rank's partial to bf16 before the cross-GPU sum get a floor of
 4e-3*max|golden| instead (up to P-1 extra roundings).
 """
@@ -45,7 +47,7 @@ def _worker(rank, world, port, out_dir):
 
     import torch.distributed as dist
 
-    from ffn_optim_b200.sharded import FusedTensorParallelFFN, RowShardedFFN, TensorParallelFFN
+    from ffn_optim_b200.sharded import FusedTensorParallelFFN, RowShardedFFN, TensorParallelFFN, TpDpFusedFFN
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -58,7 +60,7 @@ def _worker(rank, world, port, out_dir):
         out["nccl"] = tp.run().float().cpu().numpy()
         tp.check()
         out["nccl_rows"] = np.array(tp.local_rows())
-        for partial in ("fp32", "input"):
+        for partial in ("fp32", "fp24", "input"):
             fused = FusedTensorParallelFFN(x, w1, w2, partial=partial)
             first = None
             for i in range(3):  # repeated launches exercise both staging parities
@@ -74,6 +76,14 @@ def _worker(rank, world, port, out_dir):
         out["m"] = ms.run().float().cpu().numpy()
         ms.check()
         out["m_rows"] = np.arange(ms.lo, ms.hi)
+        if world >= 4:  # pairs of GPUs with the fused reduce-scatter, M split over the pairs
+            hy = TpDpFusedFFN(x, w1, w2, tp=2)
+            for _ in range(2):
+                y = hy.run()
+                hy.check()
+            out["tp2"] = y.float().cpu().numpy()
+            out["tp2_rows"] = np.array(hy.local_rows())
+            hy.close()
         np.savez(os.path.join(out_dir, f"r{rank}.npz"), **out)
         dist.barrier()
     finally:
@@ -109,14 +119,18 @@ def _worlds():
 def test_sharded_variants_vs_oracle(tmp_path, world):
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     staged, golden = _oracle()
-    seen = {k: np.zeros(SHAPE[0], dtype=bool) for k in ("nccl", "fused_fp32", "fused_input", "m")}
+    keys = ("nccl", "fused_fp32", "fused_fp24", "fused_input", "m") + (("tp2",) if world >= 4 else ())
+    seen = {k: np.zeros(SHAPE[0], dtype=bool) for k in keys}
     for r in range(world):
         d = np.load(tmp_path / f"r{r}.npz")
-        for key, floor in (("fused_fp32", 1e-3), ("m", 1e-3), ("fused_input", 4e-3), ("nccl", 4e-3)):
+        for key, floor in (("fused_fp32", 1e-3), ("fused_fp24", 1e-3), ("m", 1e-3), ("fused_input", 4e-3),
+                           ("nccl", 4e-3), ("tp2", 1e-3)):
+            if key not in keys:
+                continue
             rows = d[f"{key}_rows"]
             _check(f"{key} rank {r} of {world}", d[key], staged[rows], golden[rows], floor)
             seen[key][rows] = True
-        for partial in ("fp32", "input"):
+        for partial in ("fp32", "fp24", "input"):
             assert bool(d[f"fused_{partial}_repeat_equal"]), f"fused {partial}: run-to-run results differ"
     for key, mask in seen.items():
         assert mask.all(), f"{key}: rows not covered by any rank"

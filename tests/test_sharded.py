@@ -42,6 +42,24 @@ def test_m_slices_and_chunks():
     assert rows == list(range(65536))
 
 
+def test_tp_dp_layout():
+    from ffn_optim_b200.sharded import tp_dp_groups, tp_dp_rows
+
+    assert tp_dp_groups(8, 2) == [[0, 1], [2, 3], [4, 5], [6, 7]]
+    assert tp_dp_groups(8, 8) == [list(range(8))]
+    for bad in ((8, 3), (4, 1), (4, 8)):
+        with pytest.raises(ValueError):
+            tp_dp_groups(*bad)
+    m = 65536
+    for world, tp in ((8, 2), (8, 4), (4, 2), (2, 2)):
+        rows = [tp_dp_rows(m, world, tp, r) for r in range(world)]
+        assert rows[0][0] == 0 and rows[-1][1] == m
+        assert all(a[1] == b[0] for a, b in zip(rows, rows[1:]))  # contiguous, disjoint, in rank order
+        assert len({hi - lo for lo, hi in rows}) == 1
+    with pytest.raises(ValueError):
+        tp_dp_rows(1001, 4, 2, 0)
+
+
 def test_band_order_puts_own_band_last():
     for world in (2, 3, 8):
         for rank in range(world):
