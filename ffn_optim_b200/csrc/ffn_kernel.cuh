@@ -255,6 +255,14 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Waits until at most `keep` of this thread's newest bulk groups are pending (2, 4 or 8;
+// any other count waits for all of them).
+__device__ __forceinline__ void bulk_wait_keep(int keep) {
+  if (keep == 8) asm volatile("cp.async.bulk.wait_group 8;" ::: "memory");
+  else if (keep == 4) asm volatile("cp.async.bulk.wait_group 4;" ::: "memory");
+  else if (keep == 2) asm volatile("cp.async.bulk.wait_group 2;" ::: "memory");
+  else bulk_wait_all();
+}
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
@@ -1509,6 +1517,19 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
     }
     unsigned long long epoch = 0;  // fetched before the first flag wait or staging slot
     bool have_epoch = false;
+    // Fused reduce-scatter: the owner's count of the last pushed tile, released one tile
+    // late (lane 0) -- once the next tile's stores are issued and this one's have completed
+    // -- so the warp does not sit out an NVLink round trip per tile.  Flushed before any
+    // unit that waits on other ranks and at the end.
+    unsigned* rs_pending = nullptr;
+    auto rs_flush = [&]() {
+      if (lane == 0 && rs_pending) {
+        bulk_wait_all();
+        fence_async_global();
+        red_release_sys_add(rs_pending, 1u);
+        rs_pending = nullptr;
+      }
+    };
 #pragma unroll 1
     for (int seq = 0;; ++seq) {
       // Next unit from the ring: lane 0 waits, the warp reads the slot, lane 0 frees it.
@@ -1586,6 +1607,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
           rs_push = rs_owner != p.rs_rank;
           rs_reduce = !rs_push;
           if (rs_reduce) {
+            rs_flush();  // (other ranks' own bands may wait on it)
             // Lane `src` acquires rank src's flag (all ranks at once); the warp barrier orders
             // every lane's reads of the staged partials after those acquires.
             const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
@@ -1952,14 +1974,18 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
 
       if (rs_push) {
-        // Publish this warp's 32 rows to the owning GPU: the bulk stores complete, the async
-        // proxy is ordered before the generic one, then one system-scope release per warp on
-        // the owner's count for (this rank, tile).
+        // Publish this warp's 32 rows to the owning GPU, one tile late: the previous pushed
+        // tile's bulk stores complete (all but this tile's groups), the async proxy is
+        // ordered before the generic one, then one system-scope release per warp on that
+        // owner's count for (this rank, tile).
         const size_t band = static_cast<size_t>(p.rs_band_tiles) * p.dn.tiles_q;
         if (lane == 0) {
-          bulk_wait_all();
-          fence_async_global();
-          red_release_sys_add(p.rs_flags[rs_owner] + p.rs_rank * band + rs_tile, 1u);
+          if (rs_pending) {
+            bulk_wait_keep((p.rs_format == 0 ? 1 : 2) * kMyChunks);  // bulk groups of this tile
+            fence_async_global();
+            red_release_sys_add(rs_pending, 1u);
+          }
+          rs_pending = p.rs_flags[rs_owner] + p.rs_rank * band + rs_tile;
         }
         __syncwarp();
       }
@@ -1987,6 +2013,7 @@ __global__ void __launch_bounds__(kCtrlThreads + 32 * (EPI + (W8 ? 12 : 0)), 1)
         if (ew == 0 && lane == 0) trace_mark(p, kTrUpStored);
       }
     }
+    rs_flush();
     if constexpr (!SWAP) {
       if (lane == 0) bulk_wait_all();
       __syncwarp();
