@@ -22,6 +22,11 @@ absmax/448 (IEEE fp32 division), codes RN-even with saturation to +-448 in the O
 ("fn") format, activations entering the MMA as fp16, the kernel's fp32 sum multiplied by
 the row scale.
 
+Also beyond the reference (it is single-device): :func:`round_f24` and :func:`ffn_tp_partials`
+restate the arithmetic of this build's H-sharded multi-GPU path -- per-rank fp32 partials
+over hidden-column slices, each rounded to the wire format (fp32, 24-bit, or the input
+dtype), summed in ascending rank order, rounded once.
+
 Pinning: ``tests/golden/`` holds outputs of the reference's own ``ffn_torch`` (imported from
 the reference checkout by ``tests/golden/make_golden.py``) on the seeded inputs of each case;
 ``tests/test_oracle.py`` checks this restatement against them (at most one unit in the last
@@ -211,3 +216,35 @@ def ffn_fp8_weights(x, q1, s1, q2, s2, dtype, *, rational=True):
     hidden = round_to(gelu_rational(z) if rational else gelu_erf(z), dtype)
     y = (_as_fp16(hidden) @ w2.T) * np.asarray(s2, dtype=np.float32)
     return to_bits(y, dtype).reshape(*lead, w2.shape[0])
+
+
+def round_f24(a):
+    """fp32 values rounded to nearest (ties to even) at bit 8 of the word, the low 8 bits
+    cleared: sign, exponent and 15 explicit mantissa bits -- the 24-bit partial format of the
+    fused reduce-scatter (``partial='fp24'``; build extension).  Relative error <= 2^-16."""
+    b = np.asarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = (b + 0x7F + ((b >> 8) & 1)) & 0xFFFFFF00
+    return r.astype(np.uint32).view(np.float32)
+
+
+def ffn_tp_partials(x, w1, w2, dtype, slices, partial="fp32", *, rational=True):
+    """H-sharded FFN on len(slices) ranks: rank r's fp32 partial Y over hidden columns
+    ``slices[r] = (lo, hi)`` (GELU of the fp32 up sum, hidden rounded to ``dtype``), rounded
+    to the wire format ``partial`` ('fp32' | 'fp24' | 'input'), the partials summed in fp32 in
+    ascending rank order, then rounded once to ``dtype``.  Returns uint16 bit patterns."""
+    x = np.asarray(x, dtype=np.float32)
+    w1 = np.asarray(w1, dtype=np.float32)
+    w2 = np.asarray(w2, dtype=np.float32)
+    acc = None
+    for lo, hi in slices:
+        z = x @ w1[lo:hi].T
+        hidden = round_to(gelu_rational(z) if rational else gelu_erf(z), dtype)
+        part = (hidden @ w2[:, lo:hi].T).astype(np.float32)
+        if partial == "fp24":
+            part = round_f24(part)
+        elif partial == "input":
+            part = round_to(part, dtype)
+        elif partial != "fp32":
+            raise ValueError(partial)
+        acc = part if acc is None else (acc + part).astype(np.float32)
+    return to_bits(acc, dtype)
