@@ -168,6 +168,71 @@ def _check_hslice_cover(k, p):
     assert k["up"]["k_blocks"] == -(-p.k // 64) and k["down"]["k_blocks"] == -(-p.h // 64)
 
 
+@pytest.mark.parametrize("sm", [148, 132])
+def test_hslice_plans_fit_the_device(sm):
+    """Seeded decode shapes (M <= 16), forced and automatic: every hidden-slice plan covers
+    its blocks once, keeps every cluster resident at one CTA per SM (74 / 33 / 15 clusters of
+    2 / 4 / 8 on 148 SMs, scaled by the SM count), and its down accumulators fit TMEM beside
+    the up accumulator; automatic plans only where the clusters share H evenly."""
+    rng = np.random.Generator(np.random.PCG64(sm))
+    cap = {2: 74 * sm // 148, 4: 33 * sm // 148, 8: 15 * sm // 148}
+    seen = 0
+    for _ in range(300):
+        m = int(rng.integers(1, 17))
+        k = int(rng.integers(1, 65)) * 64
+        h = int(rng.integers(1, 400)) * 128 - int(rng.integers(0, 8)) * 8
+        n = int(rng.integers(1, 65)) * 64
+        p = problem_from_shapes([m, k], [h, k], [n, h])
+        for tile in ("hslice16", None):
+            try:
+                plan = make_plan(p, sm_count=sm, tile=tile)
+            except (NotApplicable, ValueError):
+                continue
+            kk = plan.kernel
+            if kk["variant"] != 12:
+                assert tile is None
+                continue
+            seen += 1
+            _check_hslice_cover(kk, p)
+            S = kk["row_split"]
+            CL = kk["block_num"] // S
+            nbr = -(-kk["down"]["tiles_r"] // S)
+            assert CL <= cap[S] and kk["block_num"] <= sm and nbr * 16 <= 448
+            if tile is None:
+                sb = -(-kk["up"]["tiles_r"] // S)
+                assert sb >= 2 and sb / (-(-sb // CL) * CL) >= 0.85
+    assert seen > 100
+
+
+def test_rowblock_plans_fit_the_device():
+    """Seeded shapes with N <= 512 under full_load_a: the Y accumulator is the narrowest of
+    64 / 128 / 256 columns that covers N in at most two parts, one unit per (row block,
+    part), and the cluster size S of split row blocks follows its doubling rule -- S doubles
+    (up to 8) while 2 * S * units CTAs fit the SMs and H has at least 2 * S chunks."""
+    rng = np.random.Generator(np.random.PCG64(5))
+    for _ in range(300):
+        m = int(rng.integers(1, 20000))
+        k = int(rng.integers(1, 33)) * 32
+        h = int(rng.integers(1, 65)) * 128
+        n = int(rng.integers(1, 65)) * 8
+        p = problem_from_shapes([m, k], [h, k], [n, h])
+        kk = make_plan(p, Selection(down_impl="full_load_a"), sm_count=148).kernel
+        ny = kk["tile_n"]
+        assert ny == (64 if n <= 64 else (128 if n <= 128 else 256))
+        parts = -(-n // ny)
+        assert parts <= 2
+        units = -(-m // 128) * parts
+        chunks = kk["up"]["tiles_q"]
+        assert chunks == -(-h // 128) and kk["up"]["tiles_r"] == -(-m // 128)
+        S = kk["row_split"]
+        assert S in (1, 2, 4, 8) and kk["block_num"] <= 148
+        if S > 1:  # the last doubling was allowed
+            assert kk["block_num"] == units * S and units * S <= 148 and chunks >= S
+        else:
+            assert kk["block_num"] == min(units, 148)
+        assert S == 8 or 2 * S * units > 148 or chunks < 2 * S  # and the next one was not
+
+
 @pytest.mark.parametrize("case_id", [c["case_id"] for c in C.load_cases()])
 @pytest.mark.parametrize("tile", [None, "pair256x256"])
 def test_plan_covers_every_k_block_once(case_id, tile):
