@@ -258,22 +258,51 @@ def test_plan_covers_every_k_block_once(case_id, tile):
             assert k["swap_ab"] == 1 and k["tile_n"] == 16
         elif p.m <= 64:
             assert k["swap_ab"] == 1 and k["tile_n"] == 64
-        for name in ("up", "down"):
-            ph = k[name]
-            assert ph["tiles"] == ph["tiles_r"] * ph["tiles_q"]
-            cover = {}
-            owners = {}
-            for c, t, a, b, role in _units(ph, owners_n):
-                for kb in range(a, b):
-                    cover[(t, kb)] = cover.get((t, kb), 0) + 1
-                if role in ("full", "owner"):
-                    owners[t] = owners.get(t, 0) + 1
-            assert len(cover) == ph["tiles"] * ph["k_blocks"] and set(cover.values()) == {1}
-            assert len(owners) == ph["tiles"] and set(owners.values()) == {1}
-            if ph["sk_tiles"]:
-                assert 1 <= ph["sk_ctas"] <= owners_n and ph["sk_iters"] >= 8 or ph["sk_ctas"] == 1
+        _check_cover(k, owners_n)
         if down == "basic":
             assert k["down"]["sk_tiles"] == 0
+
+
+def _check_cover(k, owners_n):
+    """Every (tile, k-block) of both phases is computed by exactly one unit and every tile
+    has exactly one owner (the CTA that finalises it)."""
+    for name in ("up", "down"):
+        ph = k[name]
+        assert ph["tiles"] == ph["tiles_r"] * ph["tiles_q"]
+        cover = {}
+        owners = {}
+        for c, t, a, b, role in _units(ph, owners_n):
+            for kb in range(a, b):
+                cover[(t, kb)] = cover.get((t, kb), 0) + 1
+            if role in ("full", "owner"):
+                owners[t] = owners.get(t, 0) + 1
+        assert len(cover) == ph["tiles"] * ph["k_blocks"] and set(cover.values()) == {1}
+        assert len(owners) == ph["tiles"] and set(owners.values()) == {1}
+        if ph["sk_tiles"]:
+            assert 1 <= ph["sk_ctas"] <= owners_n and ph["sk_iters"] >= 8 or ph["sk_ctas"] == 1
+
+
+def test_prefill_plans_cover_seeded_shapes():
+    """The k-block cover and single-owner properties on seeded ragged prefill shapes, for the
+    one-CTA and CTA-pair tiles and both down implementations (Stream-K where applicable)."""
+    rng = np.random.Generator(np.random.PCG64(9))
+    checked = 0
+    for _ in range(40):
+        m = int(rng.integers(65, 8193))
+        k_ = int(rng.integers(1, 257)) * 8
+        h = int(rng.integers(1, 1025)) * 8
+        n = int(rng.integers(1, 257)) * 8
+        p = problem_from_shapes([m, k_], [h, k_], [n, h])
+        for tile in (None, "pair256x256"):
+            for down in ("basic", "streamk"):
+                try:
+                    kk = make_plan(p, Selection(down_impl=down), sm_count=148, tile=tile).kernel
+                except NotApplicable:
+                    assert down == "streamk"
+                    continue
+                _check_cover(kk, kk["block_num"] // (2 if kk["cta_pair"] else 1))
+                checked += 1
+    assert checked >= 100
 
 
 def _claim_model(dp, C, epochs, rng):
