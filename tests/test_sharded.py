@@ -71,6 +71,61 @@ def test_band_order_puts_own_band_last():
                     assert band_order(world, other).index(rank) < world - 1
 
 
+def _rs_protocol(world, tiles, rng, flush_before_own=True):
+    """Model of the fused reduce-scatter's down phase on `world` ranks (one warp each): rank r
+    visits the bands in ``band_order``; a pushed tile's count is released one tile late (when
+    the next push is issued) and flushed before an own-band tile and at the end; an own-band
+    tile waits for every other rank's count of that tile.  Ranks step in a random order;
+    returns True when every rank finishes, False when all unfinished ranks are blocked."""
+    work = {r: [(b, j) for b in band_order(world, r) for j in range(tiles)] for r in range(world)}
+    pos = {r: 0 for r in range(world)}
+    pending = {r: None for r in range(world)}
+    released = set()  # (sender, band, tile)
+    while True:
+        live = [r for r in range(world) if pos[r] <= len(work[r])]
+        if not live:
+            return True
+        progressed = False
+        for r in rng.permutation(live):
+            r = int(r)
+            if pos[r] == len(work[r]):  # end of the work list: flush
+                if pending[r] is not None:
+                    released.add((r,) + pending[r])
+                    pending[r] = None
+                pos[r] += 1
+                progressed = True
+                continue
+            b, j = work[r][pos[r]]
+            if b != r:  # push: release the previous pushed tile, keep this one pending
+                if pending[r] is not None:
+                    released.add((r,) + pending[r])
+                pending[r] = (b, j)
+                pos[r] += 1
+                progressed = True
+            else:
+                if flush_before_own and pending[r] is not None:
+                    released.add((r,) + pending[r])
+                    pending[r] = None
+                    progressed = True
+                if all((o, r, j) in released for o in range(world) if o != r):
+                    pos[r] += 1
+                    progressed = True
+        if not progressed:
+            return False
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_deferred_push_release_is_live(world):
+    """The one-tile-late release of pushed partials cannot deadlock: with the flush before
+    own-band tiles every random interleaving finishes; without it the model finds the
+    deadlock (a rank's last push stays pending while it waits on the others)."""
+    rng = np.random.Generator(np.random.PCG64(world))
+    for tiles in (1, 2, 5):
+        for _ in range(20):
+            assert _rs_protocol(world, tiles, rng)
+    assert not all(_rs_protocol(world, tiles, rng, flush_before_own=False) for _ in range(20))
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
